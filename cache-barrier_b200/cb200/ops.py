@@ -1,0 +1,336 @@
+"""Torch-facing wrappers over the C ABI.
+
+Every function here validates shapes/dtypes, takes raw device pointers from the
+tensors, and calls into ``libcb200.so`` on the current CUDA stream. Nothing is
+computed in PyTorch; tensors are only used as device memory.
+
+Shapes: 2-D operands are a batch of one; 3-D operands are ``[batch, rows, cols]``
+as in the reference's batched kernels (profiling/bench_l2_barrier.py:102-125,
+profiling/w8a8/w8a8_bmm.py:118-140).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib as L
+
+_DTYPE_CODE = {torch.float16: L.CB_DTYPE_F16, torch.bfloat16: L.CB_DTYPE_BF16, torch.float32: L.CB_DTYPE_F32}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dt]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dt}") from None
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _strides(*vals):
+    arr = (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
+    return arr
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("all tensors must be CUDA tensors (the quantized GEMMs run only on the GPU)")
+
+
+def _as3d(t: torch.Tensor) -> torch.Tensor:
+    if t.dim() == 2:
+        return t.unsqueeze(0)
+    if t.dim() != 3:
+        raise ValueError(f"expected a 2-D or 3-D tensor, got shape {tuple(t.shape)}")
+    return t
+
+
+# ---------------------------------------------------------------------------
+# Workspace pool: one zero-initialised scratch buffer per (device, stream).
+# ---------------------------------------------------------------------------
+class WorkspacePool:
+    """Caller-owned split-K scratch for the C ABI.
+
+    Buffers are zero-filled at allocation and left zeroed by the kernels. One
+    buffer per (device, stream) so concurrent streams never share scratch. A
+    buffer first needed while a CUDA graph is being captured (torch captures on
+    its own stream) is allocated from the graph's memory pool; its zero-fill is
+    captured with it and re-runs on every replay, which keeps it valid.
+    """
+
+    def __init__(self):
+        self._bufs = {}
+        self._lock = threading.Lock()
+
+    def get(self, nbytes: int, device: torch.device) -> torch.Tensor:
+        key = (device.index, _stream(device))
+        with self._lock:
+            buf = self._bufs.get(key)
+            if buf is None or buf.numel() < nbytes:
+                size = max(nbytes, 1 << 20)
+                if buf is not None:
+                    size = max(size, 2 * buf.numel())
+                buf = torch.zeros(size, dtype=torch.uint8, device=device)
+                self._bufs[key] = buf
+            return buf
+
+    def check_status(self, device: torch.device | None = None) -> int:
+        """Synchronising read of the device status word of every buffer on device."""
+        worst = 0
+        for (idx, stream), buf in list(self._bufs.items()):
+            if device is not None and idx != device.index:
+                continue
+            st = ctypes.c_int(0)
+            code = L.load().cb_workspace_status(buf.data_ptr(), ctypes.byref(st), stream)
+            if code not in (L.CB_OK, L.CB_ERR_DEVICE_TIMEOUT):
+                L.check("cb_workspace_status", code)
+            worst |= st.value
+        return worst
+
+
+POOL = WorkspacePool()
+
+
+def workspace_bytes(op: int, batch: int, M: int, N: int, K: int) -> int:
+    return int(L.load().cb_workspace_bytes(op, batch, M, N, K))
+
+
+# ---------------------------------------------------------------------------
+# activation quantization
+# ---------------------------------------------------------------------------
+def quant_act_i8(a: torch.Tensor, q: torch.Tensor | None = None, s: torch.Tensor | None = None):
+    """Per-(batch, row) int8 quantization of ``a`` ([M, K] or [B, M, K], f16/bf16).
+
+    Returns ``(q, s)``: int8 with a's shape and fp32 scales of ``B*M`` elements
+    (the reference's flat ``[H*M]`` layout). ``q``/``s`` are filled in place
+    when given (graph-capture friendly, as profiling/w8a8/w8a8_bmm.py:92-106).
+    """
+    _require_cuda(a)
+    a3 = _as3d(a)
+    B, M, K = a3.shape
+    if a3.stride(2) != 1:
+        raise ValueError("activations must be contiguous along K")
+    if q is None:
+        q = torch.empty(a.shape, dtype=torch.int8, device=a.device)
+    if s is None:
+        s = torch.empty(B * M, dtype=torch.float32, device=a.device)
+    q3 = _as3d(q)
+    if q3.shape != a3.shape or q.dtype != torch.int8 or q3.stride(2) != 1:
+        raise ValueError("q must be an int8 tensor shaped like a, contiguous along K")
+    if s.dtype != torch.float32 or s.numel() < B * M or not s.is_contiguous():
+        raise ValueError("s must be a contiguous fp32 tensor of at least B*M elements")
+    code = L.load().cb_quant_act_i8(a3.data_ptr(), dtype_code(a.dtype), B, M, K, a3.stride(0), a3.stride(1),
+                                    q3.data_ptr(), q3.stride(0), q3.stride(1), s.data_ptr(), M, _stream(a.device))
+    L.check("cb_quant_act_i8", code)
+    return q, s
+
+
+# ---------------------------------------------------------------------------
+# W8A8
+# ---------------------------------------------------------------------------
+def w8a8_gemm(aq: torch.Tensor, w_nk: torch.Tensor, a_scale: torch.Tensor, w_scale: torch.Tensor,
+              out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
+              acc_out: torch.Tensor | None = None) -> torch.Tensor:
+    """``out = (aq @ w_nk^T)_int32 * a_scale[m] * w_scale[n]``.
+
+    aq: int8 [M, K] / [B, M, K]; w_nk: int8 [N, K] / [B, N, K] (K contiguous);
+    a_scale: fp32 with B*M elements; w_scale: fp32 [N] / [B, N].
+    """
+    _require_cuda(aq, w_nk, a_scale, w_scale, out, acc_out)
+    a3, w3 = _as3d(aq), _as3d(w_nk)
+    B, M, K = a3.shape
+    Bw, N, Kw = w3.shape
+    if aq.dtype != torch.int8 or w_nk.dtype != torch.int8:
+        raise ValueError("w8a8_gemm expects int8 operands")
+    if Kw != K or Bw != B:
+        raise ValueError(f"shape mismatch: aq {tuple(a3.shape)} vs w {tuple(w3.shape)}")
+    if a3.stride(2) != 1 or w3.stride(2) != 1:
+        raise ValueError("operands must be contiguous along K (weights K-major [N, K])")
+    if a_scale.dtype != torch.float32 or w_scale.dtype != torch.float32:
+        raise ValueError("scales must be fp32")
+    if not a_scale.is_contiguous() or a_scale.numel() < B * M:
+        raise ValueError("a_scale must be contiguous with B*M elements")
+    ws2 = w_scale.reshape(B, N) if w_scale.dim() == 1 else w_scale
+    if ws2.stride(-1) != 1:
+        raise ValueError("w_scale must be contiguous along N")
+    if out is None:
+        out = torch.empty((B, M, N) if aq.dim() == 3 else (M, N), dtype=out_dtype, device=aq.device)
+    o3 = _as3d(out)
+    if o3.shape != (B, M, N) or o3.stride(2) != 1:
+        raise ValueError("out must be [B, M, N] contiguous along N")
+    acc3 = None
+    if acc_out is not None:
+        acc3 = _as3d(acc_out)
+        if acc_out.dtype != torch.int32 or acc3.shape != o3.shape or acc3.stride() != o3.stride():
+            raise ValueError("acc_out must be int32 with out's shape and strides")
+    nbytes = workspace_bytes(L.CB_OP_W8A8, B, M, N, K)
+    ws = POOL.get(nbytes, aq.device)
+    st = _strides(a3.stride(0), a3.stride(1), w3.stride(0), w3.stride(1), o3.stride(0), o3.stride(1), M,
+                  ws2.stride(0) if ws2.dim() == 2 else 0)
+    code = L.load().cb_w8a8_gemm(a3.data_ptr(), a_scale.data_ptr(), w3.data_ptr(), ws2.data_ptr(), o3.data_ptr(),
+                                 dtype_code(out.dtype), _ptr(acc3), B, M, N, K, st, ws.data_ptr(), ws.numel(),
+                                 _stream(aq.device))
+    L.check("cb_w8a8_gemm", code)
+    return out
+
+
+def w8a8_gemm_dynamic(a: torch.Tensor, w_nk: torch.Tensor, w_scale: torch.Tensor,
+                      q: torch.Tensor | None = None, s: torch.Tensor | None = None,
+                      out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Dynamic per-token int8 quantization of ``a`` then the W8A8 GEMM (two launches, PDL-chained)."""
+    _require_cuda(a, w_nk, w_scale, q, s, out)
+    a3, w3 = _as3d(a), _as3d(w_nk)
+    B, M, K = a3.shape
+    Bw, N, Kw = w3.shape
+    if w_nk.dtype != torch.int8 or Kw != K or Bw != B:
+        raise ValueError("w_nk must be int8 [B, N, K] matching a")
+    if a3.stride(2) != 1 or w3.stride(2) != 1:
+        raise ValueError("operands must be contiguous along K")
+    if q is None:
+        q = torch.empty((B, M, K), dtype=torch.int8, device=a.device)
+    if s is None:
+        s = torch.empty(B * M, dtype=torch.float32, device=a.device)
+    if q.dtype != torch.int8 or q.numel() != B * M * K or not q.is_contiguous():
+        raise ValueError("q buffer must be contiguous int8 with B*M*K elements")
+    if s.dtype != torch.float32 or s.numel() < B * M or not s.is_contiguous():
+        raise ValueError("s buffer must be contiguous fp32 with B*M elements")
+    ws2 = w_scale.reshape(B, N) if w_scale.dim() == 1 else w_scale
+    if out is None:
+        out = torch.empty((B, M, N) if a.dim() == 3 else (M, N), dtype=out_dtype or a.dtype, device=a.device)
+    o3 = _as3d(out)
+    if o3.shape != (B, M, N) or o3.stride(2) != 1:
+        raise ValueError("out must be [B, M, N] contiguous along N")
+    nbytes = workspace_bytes(L.CB_OP_W8A8, B, M, N, K)
+    ws = POOL.get(nbytes, a.device)
+    st = _strides(a3.stride(0), a3.stride(1), w3.stride(0), w3.stride(1), o3.stride(0), o3.stride(1),
+                  ws2.stride(0) if ws2.dim() == 2 else 0)
+    code = L.load().cb_w8a8_gemm_dynamic(a3.data_ptr(), dtype_code(a.dtype), q.data_ptr(), s.data_ptr(),
+                                         w3.data_ptr(), ws2.data_ptr(), o3.data_ptr(), dtype_code(out.dtype), B, M,
+                                         N, K, st, ws.data_ptr(), ws.numel(), _stream(a.device))
+    L.check("cb_w8a8_gemm_dynamic", code)
+    return out
+
+
+def repack_w8_kmajor(w_kn: torch.Tensor) -> torch.Tensor:
+    """int8 [B, K, N] / [K, N] (N contiguous) -> contiguous [B, N, K] / [N, K]."""
+    _require_cuda(w_kn)
+    w3 = _as3d(w_kn).contiguous()
+    B, K, N = w3.shape
+    dst = torch.empty((B, N, K), dtype=torch.int8, device=w_kn.device)
+    code = L.load().cb_repack_w8_kmajor(w3.data_ptr(), dst.data_ptr(), B, K, N, _stream(w_kn.device))
+    L.check("cb_repack_w8_kmajor", code)
+    return dst if w_kn.dim() == 3 else dst[0]
+
+
+# ---------------------------------------------------------------------------
+# W4A16
+# ---------------------------------------------------------------------------
+def w4_native_bytes(batch: int, K: int, N: int) -> int:
+    return int(L.load().cb_w4_native_bytes(batch, K, N))
+
+
+def repack_w4(src: torch.Tensor, layout: int, K: int, N: int) -> torch.Tensor:
+    """Repack int4 weights (reference u8 [B, K/2, N] or int32 [B, K/8, N]) into the native tiled layout."""
+    _require_cuda(src)
+    s3 = _as3d(src).contiguous()
+    B = s3.shape[0]
+    if layout == L.CB_W4_REF_U8_KN:
+        if src.dtype != torch.uint8 or s3.shape[1:] != (K // 2, N):
+            raise ValueError("reference int4 layout is uint8 [B, K/2, N]")
+    elif layout == L.CB_W4_I32_K8N:
+        if src.dtype != torch.int32 or s3.shape[1:] != (K // 8, N):
+            raise ValueError("int32 int4 layout is int32 [B, K/8, N]")
+    else:
+        raise ValueError(f"unknown source layout {layout}")
+    dst = torch.empty(w4_native_bytes(B, K, N), dtype=torch.uint8, device=src.device)
+    code = L.load().cb_repack_w4(s3.data_ptr(), layout, dst.data_ptr(), B, K, N, _stream(src.device))
+    L.check("cb_repack_w4", code)
+    return dst
+
+
+def w4a16_gemm(a: torch.Tensor, w_native: torch.Tensor, scales: torch.Tensor, N: int, group_size: int,
+               out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
+               scale_strides: tuple[int, int] | None = None) -> torch.Tensor:
+    """``out[b, m, n] = sum_k a[b, m, k] * q[b, k, n] * scales[b, k // group_size, n]``.
+
+    a: f16/bf16 [M, K] / [B, M, K]; w_native: uint8 from ``repack_w4``;
+    scales: [G, N] / [B, G, N] (f16/bf16/f32), N contiguous, or [B, N] for the
+    per-channel case (group_size >= K). ``scale_strides`` overrides the
+    (batch, group) element strides of ``scales``.
+    """
+    _require_cuda(a, w_native, scales, out)
+    a3 = _as3d(a)
+    B, M, K = a3.shape
+    if a3.stride(2) != 1:
+        raise ValueError("activations must be contiguous along K")
+    if w_native.dtype != torch.uint8 or w_native.numel() < w4_native_bytes(B, K, N):
+        raise ValueError("w_native must be a uint8 native-layout buffer for [B, K, N]")
+    if scales.stride(-1) != 1:
+        raise ValueError("scales must be contiguous along N")
+    if scale_strides is not None:
+        s_sb, s_sg = scale_strides
+    elif scales.dim() == 3:
+        s_sb, s_sg = scales.stride(0), scales.stride(1)
+    elif scales.dim() == 2:
+        if group_size >= K:  # per-(batch, channel) scales [B, N], the reference layout
+            s_sb, s_sg = scales.stride(0), 0
+        else:  # [G, N] for a batch of one
+            s_sb, s_sg = 0, scales.stride(0)
+    else:
+        s_sb, s_sg = 0, 0
+    if out is None:
+        out = torch.empty((B, M, N) if a.dim() == 3 else (M, N), dtype=out_dtype or a.dtype, device=a.device)
+    o3 = _as3d(out)
+    if o3.shape != (B, M, N) or o3.stride(2) != 1:
+        raise ValueError("out must be [B, M, N] contiguous along N")
+    nbytes = workspace_bytes(L.CB_OP_W4A16, B, M, N, K)
+    ws = POOL.get(nbytes, a.device)
+    st = _strides(a3.stride(0), a3.stride(1), s_sb, s_sg, o3.stride(0), o3.stride(1))
+    code = L.load().cb_w4a16_gemm(a3.data_ptr(), dtype_code(a.dtype), w_native.data_ptr(), scales.data_ptr(),
+                                  dtype_code(scales.dtype), group_size, o3.data_ptr(), dtype_code(out.dtype), B, M,
+                                  N, K, st, ws.data_ptr(), ws.numel(), _stream(a.device))
+    L.check("cb_w4a16_gemm", code)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# W4A4
+# ---------------------------------------------------------------------------
+def w4a4_gemm(a_packed: torch.Tensor, b_packed: torch.Tensor, K: int, out: torch.Tensor | None = None,
+              reference_wrap: bool = False):
+    """fp32 ``C = int4(A) @ int4(B)``; A uint8 [M, K/2], B uint8 [K/2, N].
+
+    Nibbles are two's complement int4 unless ``reference_wrap``, which reproduces
+    the reference kernel's uint8 arithmetic (negative nibbles enter as 240..255,
+    kernels/triton_gemm.py:164-167)."""
+    _require_cuda(a_packed, b_packed, out)
+    M = a_packed.shape[0]
+    N = b_packed.shape[1]
+    if a_packed.stride(1) != 1 or b_packed.stride(1) != 1:
+        raise ValueError("packed operands must be row-contiguous")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=a_packed.device)
+    nbytes = workspace_bytes(L.CB_OP_W4A4, 1, M, N, K)
+    ws = POOL.get(nbytes, a_packed.device)
+    code = L.load().cb_w4a4_gemm(a_packed.data_ptr(), b_packed.data_ptr(), out.data_ptr(), M, N, K,
+                                 a_packed.stride(0), b_packed.stride(0), out.stride(0),
+                                 L.CB_W4A4_REF_UINT8_WRAP if reference_wrap else L.CB_W4A4_SIGNED,
+                                 ws.data_ptr(), ws.numel(),
+                                 _stream(a_packed.device))
+    L.check("cb_w4a4_gemm", code)
+    return out
+
+
+def device_status(device: torch.device | None = None) -> int:
+    """Synchronising check of the kernels' device-side status words (0 = no timeout)."""
+    return POOL.check_status(device)

@@ -1,0 +1,55 @@
+// Shared pieces of the split-K ("stream-K") GEMM kernels.
+//
+// Work decomposition: an output tile is (batch h, 128 rows of N, TN tokens of M).
+// Each tile needs KB k-blocks. All tiles' k-blocks are laid end to end
+// (tile-major) and cut into G equal contiguous ranges, one per CTA, so every SM
+// streams the same number of weight bytes whatever the shape. A tile whose
+// k-blocks fall in one CTA's range is finished by that CTA; a tile cut by a
+// range boundary is reduced deterministically: each contributor writes its
+// partial accumulator to its own slot, and the last one to arrive (per-tile
+// arrival counter) sums the slots in CTA order and runs the epilogue.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "cb200.h"
+
+namespace cb {
+
+struct StreamK {
+  long long total;  // tiles * kb_per_tile
+  int grid;         // number of CTAs
+  int kb_per_tile;
+
+  __host__ __device__ long long start(int c) const { return static_cast<long long>(c) * total / grid; }
+  // CTA whose range holds global k-block g.
+  __host__ __device__ int owner(long long g) const {
+    return static_cast<int>(((g + 1) * grid - 1) / total);
+  }
+  // Slot kind of CTA c's contribution to tile t: 0 if the contribution is the
+  // first segment of c's range, 1 if it is the last one.
+  __host__ __device__ int kind(int c, long long tile) const {
+    return start(c) >= tile * kb_per_tile ? 0 : 1;
+  }
+};
+
+// Output element store for the runtime-selected dtype.
+__device__ __forceinline__ void store_elem(void* out, int dtype, long long idx, float v) {
+  if (dtype == CB_DTYPE_BF16) {
+    reinterpret_cast<__nv_bfloat16*>(out)[idx] = __float2bfloat16_rn(v);
+  } else if (dtype == CB_DTYPE_F16) {
+    reinterpret_cast<__half*>(out)[idx] = __float2half_rn(v);
+  } else {
+    reinterpret_cast<float*>(out)[idx] = v;
+  }
+}
+
+__device__ __forceinline__ float load_elem(const void* p, int dtype, long long idx) {
+  if (dtype == CB_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[idx]);
+  if (dtype == CB_DTYPE_F16) return __half2float(reinterpret_cast<const __half*>(p)[idx]);
+  return reinterpret_cast<const float*>(p)[idx];
+}
+
+}  // namespace cb

@@ -1,0 +1,99 @@
+// Host-side internals shared by the kernel launchers and the C-ABI layer.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "cb200.h"
+
+namespace cb {
+
+constexpr int kMaxStages = 16;
+constexpr size_t kWsHeader = 256;  // status word + padding
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// SM count of the current device (cached per device); 0 if no device.
+int sm_count();
+
+// Token tile (MMA N) for M tokens: 16, 32, 64, 128 or 256.
+inline int token_tile(int64_t M) {
+  if (M <= 16) return 16;
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  return 256;
+}
+
+// Split-K scratch carved out of the caller's workspace.
+struct Workspace {
+  int* status;
+  int* counters;
+  void* partials;
+};
+
+inline size_t workspace_need(int grid, size_t slot_bytes) {
+  return kWsHeader + align_up(static_cast<size_t>(grid) * sizeof(int), 256) + 2 * static_cast<size_t>(grid) * slot_bytes;
+}
+
+inline Workspace carve_workspace(void* ws, int grid) {
+  Workspace w;
+  char* base = static_cast<char*>(ws);
+  w.status = reinterpret_cast<int*>(base);
+  w.counters = reinterpret_cast<int*>(base + kWsHeader);
+  w.partials = base + kWsHeader + align_up(static_cast<size_t>(grid) * sizeof(int), 256);
+  return w;
+}
+
+// 3-D tiled tensor map (dims innermost first; strides of dims 1, 2 in elements).
+int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t d0, uint64_t d1,
+                   uint64_t d2, uint64_t stride1_elems, uint64_t stride2_elems, uint32_t box0, uint32_t box1,
+                   CUtensorMapSwizzle swizzle);
+
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? CB_OK : CB_ERR_CUDA; }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- launchers (validated arguments) ----
+int launch_act_quant(const void* a, int a_dtype, int64_t batch, int64_t M, int64_t K, int64_t a_sb, int64_t a_sm,
+                     int8_t* q, int64_t q_sb, int64_t q_sm, float* scale, int64_t s_sb, cudaStream_t stream);
+
+struct W8A8Launch {
+  const int8_t* aq;
+  const float* a_scale;
+  const int8_t* w;
+  const float* w_scale;
+  void* out;
+  int out_dtype;
+  int32_t* acc_out;
+  int64_t batch, M, N, K;
+  int64_t aq_sb, aq_sm, w_sb, w_sn, out_sb, out_sm, as_sb, ws_sb;
+  int raw_f32;            // 1: out = (float)acc, no scales (W4A4 path)
+  int unsigned_operands;  // 1: both operands are uint8 (W4A4 reference-wrap mode)
+  void* workspace;
+  size_t workspace_bytes;
+};
+int launch_w8a8(const W8A8Launch& L, cudaStream_t stream);
+size_t w8a8_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K);
+
+struct W4A16Launch {
+  const void* a;
+  int a_dtype;
+  const uint8_t* w;
+  const void* scales;
+  int scale_dtype;
+  int64_t group_size;
+  void* out;
+  int out_dtype;
+  int64_t batch, M, N, K;
+  int64_t a_sb, a_sm, s_sb, s_sg, out_sb, out_sm;
+  void* workspace;
+  size_t workspace_bytes;
+};
+int launch_w4a16(const W4A16Launch& L, cudaStream_t stream);
+size_t w4a16_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K);
+
+}  // namespace cb

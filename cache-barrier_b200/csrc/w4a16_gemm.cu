@@ -1,0 +1,546 @@
+// W4A16 int4 group-dequant GEMM (and batched INT4 BMM) for sm_100a.
+//
+// Math: out[h, m, n] = sum_k a[h, m, k] * q[h, k, n] * s[h, k / G, n]
+// following kernel_batched_w4a16_simple (profiling/bench_l2_barrier.py:36-85),
+// whose per-output-channel scale is the single-group case G = K; the reference
+// applies that scale once to the fp32 accumulator (:80-82), and so does this
+// kernel when G >= K. For G = 128 (one group per k-block) the scale is folded
+// into the dequantized weight before the MMA.
+//
+// Data path per k-block (128 rows of N x 128 of K):
+//   1. warp 0 copies the 8 KiB native weight tile with one cp.async.bulk and the
+//      token tile (TN x 128 activations, two 128-byte-swizzled TMA boxes);
+//   2. a dequant warpgroup (4 warps, one weight row per thread) reads its row's
+//      64 bytes from shared memory, turns nibbles into bf16/f16 pairs with one
+//      LOP3 (mask + exponent-bias OR + sign flip) and one packed subtract, applies
+//      the group scale, and writes the 128 values straight into TMEM with
+//      tcgen05.st — the dequantized operand never goes back through shared
+//      memory;
+//   3. warp 1 issues 8 tcgen05.mma kind::f16 (K = 16 each) with A read from TMEM
+//      and B (tokens) from shared memory, accumulating fp32 in TMEM.
+// Two dequant warpgroups alternate k-blocks over four TMEM A buffers; the first
+// group also runs the epilogue. Split-K and the deterministic reduction are the
+// stream-K scheme of cb_gemm_common.cuh.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <type_traits>
+
+#include "cb_gemm_common.cuh"
+#include "cb_internal.h"
+#include "cb_ptx.cuh"
+
+namespace cb {
+namespace {
+
+constexpr int kBlockN = 128;
+constexpr int kBlockK = 128;
+constexpr int kThreads = 320;  // producer, MMA, 2 x 4 dequant warps
+constexpr uint32_t kWTileBytes = kBlockN * kBlockK / 2;  // 8 KiB
+constexpr int kNumABuf = 4;
+constexpr uint32_t kACols = kBlockK / 2;  // 32-bit TMEM columns per A buffer (2 x 16-bit per column)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kDCol = kNumABuf * kACols;  // accumulator starts after the A buffers
+
+struct Params {
+  int M, N, K, H;
+  int n_tiles, m_tiles, kb_per_tile;
+  int stages;
+  StreamK sk;
+  const uint8_t* w;  // native tiles
+  const void* scales;
+  int scale_dtype;
+  long long s_sb, s_sg;
+  int group_size;
+  int scale_in_epilogue;
+  void* out;
+  int out_dtype;
+  long long out_sb, out_sm;
+  float* partials;  // [grid][2][TN][128]
+  int* counters;
+  int* status;
+};
+
+template <typename T>
+struct Dq;
+template <>
+struct Dq<__nv_bfloat16> {
+  using T2 = __nv_bfloat162;
+  // 0x4300 = 128.0; nibble (offset by 8) lands in the low mantissa bits.
+  static constexpr uint32_t kOrXor = 0x43084308u;
+  static __device__ __forceinline__ T2 bias() { return __floats2bfloat162_rn(136.0f, 136.0f); }
+  static __device__ __forceinline__ T2 from_f(float f) { return __float2bfloat162_rn(f); }
+};
+template <>
+struct Dq<__half> {
+  using T2 = __half2;
+  // 0x6400 = 1024.0 in f16; ulp 1 in [1024, 2048).
+  static constexpr uint32_t kOrXor = 0x64086408u;
+  static __device__ __forceinline__ T2 bias() { return __floats2half2_rn(1032.0f, 1032.0f); }
+  static __device__ __forceinline__ T2 from_f(float f) { return __float2half2_rn(f); }
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t dq_pair(uint32_t word, int shift, typename Dq<T>::T2 bias,
+                                            typename Dq<T>::T2 sc, bool apply_scale) {
+  using T2 = typename Dq<T>::T2;
+  uint32_t bits = ((word >> shift) & 0x000F000Fu) ^ Dq<T>::kOrXor;
+  T2 v = *reinterpret_cast<T2*>(&bits);
+  v = __hsub2(v, bias);
+  if (apply_scale) v = __hmul2(v, sc);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void decode_tile(const Params& p, long long tile, int& h, int& nt, int& mt) {
+  mt = static_cast<int>(tile % p.m_tiles);
+  long long r = tile / p.m_tiles;
+  nt = static_cast<int>(r % p.n_tiles);
+  h = static_cast<int>(r / p.n_tiles);
+}
+
+__device__ __forceinline__ void emit_row(const Params& p, int h, int n, int m0, int t0, const float (&v)[16]) {
+  if (n >= p.N) return;
+  const float sc = p.scale_in_epilogue ? load_elem(p.scales, p.scale_dtype, h * p.s_sb + n) : 1.0f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int m = m0 + t0 + j;
+    if (m < p.M) {
+      const long long idx = h * p.out_sb + static_cast<long long>(m) * p.out_sm + n;
+      const float f = p.scale_in_epilogue ? __fmul_rn(v[j], sc) : v[j];
+      store_elem(p.out, p.out_dtype, idx, f);
+    }
+  }
+}
+
+template <typename T, int TN>
+__global__ void __launch_bounds__(kThreads, 1)
+    w4a16_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const Params p) {
+  constexpr uint32_t kATileBytes = TN * kBlockK * 2;  // two 128-byte-swizzled boxes of TN x 64
+  constexpr uint32_t kBoxBytes = TN * 128;
+  constexpr uint32_t kStageBytes = kWTileBytes + kATileBytes;
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[kMaxStages];
+  __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+  __shared__ __align__(8) uint64_t afull_bar[kNumABuf];
+  __shared__ __align__(8) uint64_t aempty_bar[kNumABuf];
+  __shared__ __align__(8) uint64_t tfull_bar, tempty_bar, drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag;
+  __shared__ int sh_issued, sh_consumed, sh_is_last;
+  volatile int* abort_ptr = &abort_flag;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_a = smem;                              // token tiles (1024-aligned)
+  uint8_t* smem_w = smem + p.stages * kATileBytes;     // weight tiles
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int S = p.stages;
+  const int KB = p.kb_per_tile;
+  const long long g0 = p.sk.start(blockIdx.x);
+  const long long g1 = p.sk.start(blockIdx.x + 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 5);  // 4 dequant warps + 1 MMA commit
+    }
+    for (int b = 0; b < kNumABuf; ++b) {
+      mbar_init(&afull_bar[b], 4);
+      mbar_init(&aempty_bar[b], 1);
+    }
+    mbar_init(&tfull_bar, 1);
+    mbar_init(&tempty_bar, 4);
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    sh_issued = 0;
+    sh_consumed = 0;
+    sh_is_last = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_a);
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(&tmem_base_sh, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+  const uint32_t tmem_d = tmem_base + kDCol;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer ----------------
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_a = policy_evict_last();
+      const long long nmine = g1 - g0;
+      const int pro = static_cast<int>(nmine < S ? nmine : S);
+      for (int j = 0; j < pro; ++j) {
+        const long long g = g0 + j;
+        const long long tile = g / KB;
+        const int kb = static_cast<int>(g % KB);
+        int h, nt, mt;
+        decode_tile(p, tile, h, nt, mt);
+        const uint8_t* src = p.w + ((static_cast<long long>(h) * p.n_tiles + nt) * KB + kb) * kWTileBytes;
+        mbar_arrive_expect_tx(&full_bar[j], kStageBytes);
+        bulk_copy_g2s(smem_w + j * kWTileBytes, src, kWTileBytes, &full_bar[j], pol_w);
+      }
+      pdl_wait_primary();
+      for (int j = 0; j < pro; ++j) {
+        const long long g = g0 + j;
+        const long long tile = g / KB;
+        const int kb = static_cast<int>(g % KB);
+        int h, nt, mt;
+        decode_tile(p, tile, h, nt, mt);
+        uint8_t* dst = smem_a + j * kATileBytes;
+        tma_load_3d(dst, &tmap_a, &full_bar[j], kb * kBlockK, mt * TN, h, pol_a);
+        tma_load_3d(dst + kBoxBytes, &tmap_a, &full_bar[j], kb * kBlockK + 64, mt * TN, h, pol_a);
+      }
+      int issued = pro;
+      int stage = pro % S;
+      uint32_t phase = (pro == S) ? 1u : 0u;
+      for (long long g = g0 + pro; g < g1; ++g) {
+        if (*abort_ptr || !mbar_wait(&empty_bar[stage], phase ^ 1u, abort_ptr, p.status)) break;
+        const long long tile = g / KB;
+        const int kb = static_cast<int>(g % KB);
+        int h, nt, mt;
+        decode_tile(p, tile, h, nt, mt);
+        const uint8_t* src = p.w + ((static_cast<long long>(h) * p.n_tiles + nt) * KB + kb) * kWTileBytes;
+        mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+        bulk_copy_g2s(smem_w + stage * kWTileBytes, src, kWTileBytes, &full_bar[stage], pol_w);
+        uint8_t* dst = smem_a + stage * kATileBytes;
+        tma_load_3d(dst, &tmap_a, &full_bar[stage], kb * kBlockK, mt * TN, h, pol_a);
+        tma_load_3d(dst + kBoxBytes, &tmap_a, &full_bar[stage], kb * kBlockK + 64, mt * TN, h, pol_a);
+        ++issued;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      sh_issued = issued;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = idesc_f16_f32(kBlockN, TN, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
+      uint32_t acc_phase = 0;
+      int consumed = 0;
+      bool ok = true;
+      long long g = g0;
+      while (g < g1 && ok) {
+        const long long tile = g / KB;
+        const long long seg_end = (tile + 1) * KB < g1 ? (tile + 1) * KB : g1;
+        if (!mbar_wait(&tempty_bar, acc_phase ^ 1u, abort_ptr, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        bool first = true;
+        for (; g < seg_end; ++g) {
+          const int j = static_cast<int>(g - g0);
+          const int s = j % S;
+          const uint32_t ph = static_cast<uint32_t>((j / S) & 1);
+          const int b = j & (kNumABuf - 1);
+          const uint32_t aph = static_cast<uint32_t>((j >> 2) & 1);
+          if (*abort_ptr || !mbar_wait(&full_bar[s], ph, abort_ptr, p.status) ||
+              !mbar_wait(&afull_bar[b], aph, abort_ptr, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem_a + s * kATileBytes);
+          const uint32_t a_tmem = tmem_base + b * kACols;
+#pragma unroll
+          for (int i = 0; i < kBlockK / 16; ++i) {
+            const uint32_t baddr = a_base + (i >> 2) * kBoxBytes + (i & 3) * 32;
+            mma_f16_ts(tmem_d, a_tmem + i * 8, smem_desc_sw128(baddr), idesc, (first && i == 0) ? 0u : 1u);
+          }
+          first = false;
+          mma_commit(&aempty_bar[b]);
+          mma_commit(&empty_bar[s]);
+          ++consumed;
+        }
+        if (!ok) break;
+        mma_commit(&tfull_bar);
+        acc_phase ^= 1u;
+      }
+      sh_consumed = consumed;
+      mma_commit(&drain_bar);
+      mbar_wait(&drain_bar, 0, nullptr, p.status);
+    }
+  } else {
+    // ---------------- dequant warpgroups (warps 2-5: group 0, 6-9: group 1) ----------------
+    // Control flow stays uniform after an aborted wait (work is skipped, every
+    // barrier arrival and named barrier still happens), so no warp is left
+    // waiting on a collective that another warp abandoned.
+    const int grp = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const typename Dq<T>::T2 bias = Dq<T>::bias();
+    const bool fold_scale = !p.scale_in_epilogue;
+    pdl_wait_primary();
+    uint32_t acc_phase = 0;
+    long long g = g0;
+    while (g < g1) {
+      const long long tile = g / KB;
+      const int kb0 = static_cast<int>(g - tile * KB);
+      const long long seg_end = (tile + 1) * KB < g1 ? (tile + 1) * KB : g1;
+      const int kb1 = static_cast<int>(seg_end - tile * KB);
+      const bool first_seg = (g == g0);
+      int h, nt, mt;
+      decode_tile(p, tile, h, nt, mt);
+      const int n = nt * kBlockN + row;
+      for (long long gg = g; gg < seg_end; ++gg) {
+        const int j = static_cast<int>(gg - g0);
+        if ((j & 1) != grp) continue;
+        const int s = j % S;
+        const uint32_t ph = static_cast<uint32_t>((j / S) & 1);
+        const int b = j & (kNumABuf - 1);
+        const uint32_t aph = static_cast<uint32_t>((j >> 2) & 1);
+        bool got = mbar_wait(&full_bar[s], ph, abort_ptr, p.status);
+        got = mbar_wait(&aempty_bar[b], aph ^ 1u, abort_ptr, p.status) && got;
+        const bool live = __all_sync(0xffffffffu, got);
+        if (live) {
+          tc_fence_after();
+          typename Dq<T>::T2 sc = Dq<T>::from_f(1.0f);
+          if (fold_scale) {
+            const int kb = static_cast<int>(gg - tile * KB);
+            const long long gi = static_cast<long long>(kb) * kBlockK / p.group_size;
+            const float sv = n < p.N ? load_elem(p.scales, p.scale_dtype, h * p.s_sb + gi * p.s_sg + n) : 0.0f;
+            sc = Dq<T>::from_f(sv);
+          }
+          const uint4* wrow = reinterpret_cast<const uint4*>(smem_w + s * kWTileBytes + row * 64);
+          const int swz = (row >> 1) & 3;
+          const uint32_t a_addr = tmem_base + lane_off + b * kACols;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 v = wrow[c ^ swz];
+            uint32_t r[16];
+            const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+#pragma unroll
+              for (int pi = 0; pi < 4; ++pi) r[wi * 4 + pi] = dq_pair<T>(words[wi], 4 * pi, bias, sc, fold_scale);
+            }
+            __syncwarp();
+            tmem_st16(a_addr + c * 16, r);
+          }
+          tmem_st_wait();
+          tc_fence_before();
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&afull_bar[b]);
+          mbar_arrive(&empty_bar[s]);
+        }
+      }
+      g = seg_end;
+      if (grp != 0) continue;
+
+      // ---------------- epilogue (group 0) ----------------
+      const bool got = mbar_wait(&tfull_bar, acc_phase, abort_ptr, p.status);
+      acc_phase ^= 1u;
+      const bool live = __all_sync(0xffffffffu, got);
+      tc_fence_after();
+      const int m0 = mt * TN;
+      const uint32_t d_addr = tmem_d + lane_off;
+      if (kb0 == 0 && kb1 == KB) {
+        if (live) {
+#pragma unroll 1
+          for (int c = 0; c < TN / 16; ++c) {
+            uint32_t r[16];
+            __syncwarp();
+            tmem_ld16(d_addr + c * 16, r);
+            tmem_ld_wait();
+            float v[16];
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) v[jj] = __uint_as_float(r[jj]);
+            emit_row(p, h, n, m0, c * 16, v);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar);
+      } else {
+        const int slot = blockIdx.x * 2 + (first_seg ? 0 : 1);
+        float* dst = p.partials + static_cast<long long>(slot) * TN * kBlockN;
+        if (live) {
+#pragma unroll 1
+          for (int c = 0; c < TN / 16; ++c) {
+            uint32_t r[16];
+            __syncwarp();
+            tmem_ld16(d_addr + c * 16, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) dst[(c * 16 + jj) * kBlockN + row] = __uint_as_float(r[jj]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar);
+        __threadfence();
+        named_bar_sync(1, 128);
+        const int c_first = p.sk.owner(tile * KB);
+        const int c_last = p.sk.owner((tile + 1) * KB - 1);
+        if (threadIdx.x == 64) {
+          int last = 0;
+          if (!*abort_ptr) {  // an aborted CTA never publishes an incomplete slot
+            const int prev = atomicAdd(&p.counters[c_first], 1);
+            last = (prev == c_last - c_first) ? 1 : 0;
+          }
+          sh_is_last = last;
+        }
+        named_bar_sync(1, 128);
+        if (sh_is_last) {
+          __threadfence();
+#pragma unroll 1
+          for (int c = 0; c < TN / 16; ++c) {
+            float v[16];
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) v[jj] = 0.0f;
+            for (int cc = c_first; cc <= c_last; ++cc) {
+              const int sl = cc * 2 + p.sk.kind(cc, tile);
+              const float* src = p.partials + static_cast<long long>(sl) * TN * kBlockN;
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) v[jj] = __fadd_rn(v[jj], __ldcg(src + (c * 16 + jj) * kBlockN + row));
+            }
+            emit_row(p, h, n, m0, c * 16, v);
+          }
+          named_bar_sync(1, 128);
+          if (threadIdx.x == 64) p.counters[c_first] = 0;
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && abort_flag) {
+    for (int j = sh_consumed; j < sh_issued; ++j) mbar_wait(&full_bar[j % S], (j / S) & 1, nullptr, p.status);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+template <typename T, int TN>
+int launch_typed(const W4A16Launch& L, cudaStream_t stream, int grid, int stages, const Params& prm) {
+  CUtensorMap ta;
+  const CUtensorMapDataType dt =
+      (L.a_dtype == CB_DTYPE_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  int st = encode_tmap_3d(&ta, dt, L.a, static_cast<uint64_t>(L.K), static_cast<uint64_t>(L.M),
+                          static_cast<uint64_t>(L.batch), L.a_sm, L.a_sb, 64, TN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != CB_OK) return st;
+  const size_t smem = static_cast<size_t>(stages) * (kWTileBytes + TN * kBlockK * 2) + 1024;
+  static thread_local int configured_dev = -1;
+  static thread_local size_t configured_smem = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev || configured_smem < smem) {
+    cudaError_t e = cudaFuncSetAttribute(w4a16_gemm_kernel<T, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return CB_ERR_CUDA;
+    configured_dev = dev;
+    configured_smem = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, w4a16_gemm_kernel<T, TN>, ta, prm));
+}
+
+template <typename T>
+int launch_dtype(const W4A16Launch& L, cudaStream_t stream, int TN, int grid, int stages, const Params& p) {
+  switch (TN) {
+    case 16:
+      return launch_typed<T, 16>(L, stream, grid, stages, p);
+    case 32:
+      return launch_typed<T, 32>(L, stream, grid, stages, p);
+    case 64:
+      return launch_typed<T, 64>(L, stream, grid, stages, p);
+    case 128:
+      return launch_typed<T, 128>(L, stream, grid, stages, p);
+    default:
+      return launch_typed<T, 256>(L, stream, grid, stages, p);
+  }
+}
+
+}  // namespace
+
+size_t w4a16_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K) {
+  (void)batch;
+  (void)N;
+  (void)K;
+  int sms = sm_count();
+  if (sms <= 0) sms = 148;
+  return workspace_need(sms, static_cast<size_t>(token_tile(M)) * kBlockN * sizeof(float));
+}
+
+int launch_w4a16(const W4A16Launch& L, cudaStream_t stream) {
+  const int TN = token_tile(L.M);
+  Params p = {};
+  p.M = static_cast<int>(L.M);
+  p.N = static_cast<int>(L.N);
+  p.K = static_cast<int>(L.K);
+  p.H = static_cast<int>(L.batch);
+  p.n_tiles = static_cast<int>((L.N + kBlockN - 1) / kBlockN);
+  p.m_tiles = static_cast<int>((L.M + TN - 1) / TN);
+  p.kb_per_tile = static_cast<int>((L.K + kBlockK - 1) / kBlockK);
+  const long long tiles = static_cast<long long>(p.H) * p.n_tiles * p.m_tiles;
+  const long long total = tiles * p.kb_per_tile;
+  const int sms = sm_count();
+  if (sms <= 0) return CB_ERR_CUDA;
+  const int grid = static_cast<int>(total < sms ? total : sms);
+  const size_t need = workspace_need(grid, static_cast<size_t>(TN) * kBlockN * sizeof(float));
+  if (L.workspace == nullptr || L.workspace_bytes < need) return CB_ERR_WORKSPACE;
+  const size_t stage_bytes = kWTileBytes + static_cast<size_t>(TN) * kBlockK * 2;
+  int stages = static_cast<int>((200u * 1024u) / stage_bytes);
+  if (stages > kMaxStages) stages = kMaxStages;
+  if (stages < 2) stages = 2;
+  p.stages = stages;
+  p.sk.total = total;
+  p.sk.grid = grid;
+  p.sk.kb_per_tile = p.kb_per_tile;
+  p.w = L.w;
+  p.scales = L.scales;
+  p.scale_dtype = L.scale_dtype;
+  p.s_sb = L.s_sb;
+  p.s_sg = L.s_sg;
+  p.group_size = static_cast<int>(L.group_size);
+  p.scale_in_epilogue = L.group_size >= L.K ? 1 : 0;
+  p.out = L.out;
+  p.out_dtype = L.out_dtype;
+  p.out_sb = L.out_sb;
+  p.out_sm = L.out_sm;
+  Workspace ws = carve_workspace(L.workspace, grid);
+  p.partials = static_cast<float*>(ws.partials);
+  p.counters = ws.counters;
+  p.status = ws.status;
+  if (L.a_dtype == CB_DTYPE_BF16) return launch_dtype<__nv_bfloat16>(L, stream, TN, grid, stages, p);
+  return launch_dtype<__half>(L, stream, TN, grid, stages, p);
+}
+
+}  // namespace cb

@@ -1,0 +1,446 @@
+// W8A8 INT8 GEMM for sm_100a: TMA -> shared memory ring -> tcgen05.mma kind::i8
+// (int32 accumulators in TMEM) -> fused per-token x per-channel epilogue.
+//
+// Math follows _w8a8_bmm_kernel (profiling/w8a8/w8a8_bmm.py:44-81):
+//   acc[m, n] = sum_k aq[m, k] * w[k, n]            (int32, exact)
+//   out[m, n] = cvt(((float)acc * a_scale[m]) * w_scale[n])
+//
+// Orientation ("swap-AB"): the weight tile is the MMA's M = 128 operand (rows =
+// output channels n, K-major) and the token tile is the MMA's N = TN operand, so
+// decode batches of 1..32 tokens still fill 128-row MMAs. Work is split over
+// all SMs with the stream-K partition of cb_gemm_common.cuh.
+//
+// Warp roles (192 threads):
+//   warp 0     TMA producer (one lane): weight tile 128 x 128 B + token tile TN x 128 B
+//              per k-block, 128-byte swizzle. Weight loads of the first ring pass
+//              are issued before griddepcontrol.wait; token loads after it.
+//   warp 1     TMEM allocation + MMA issuer (one lane), 4 MMAs (K = 32) per k-block.
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator, scaling, bf16/f16/f32
+//              stores, split-K slot writes and the deterministic reduction.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "cb_gemm_common.cuh"
+#include "cb_internal.h"
+#include "cb_ptx.cuh"
+
+namespace cb {
+namespace {
+
+constexpr int kBlockN = 128;   // weight rows per tile (MMA M)
+constexpr int kBlockK = 128;   // int8 K per k-block (one 128-byte swizzle row)
+constexpr int kThreads = 192;
+constexpr uint32_t kWTileBytes = kBlockN * kBlockK;
+
+struct Params {
+  int M, N, K, H;
+  int n_tiles, m_tiles, kb_per_tile;
+  int stages;
+  StreamK sk;
+  const float* a_scale;
+  long long as_sb;
+  const float* w_scale;
+  long long ws_sb;
+  void* out;
+  int out_dtype;
+  long long out_sb, out_sm;
+  int32_t* acc_out;
+  int raw_f32;
+  int32_t* partials;  // [grid][2][TN][128]
+  int* counters;      // [grid]
+  int* status;
+};
+
+__device__ __forceinline__ void decode_tile(const Params& p, long long tile, int& h, int& nt, int& mt) {
+  mt = static_cast<int>(tile % p.m_tiles);
+  long long r = tile / p.m_tiles;
+  nt = static_cast<int>(r % p.n_tiles);
+  h = static_cast<int>(r / p.n_tiles);
+}
+
+template <int TN>
+__device__ __forceinline__ void emit_row(const Params& p, int h, int n, int m0, int t0, const int32_t (&v)[16]) {
+  if (n >= p.N) return;
+  const float ws = p.raw_f32 ? 1.0f : p.w_scale[h * p.ws_sb + n];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int m = m0 + t0 + j;
+    if (m < p.M) {
+      const long long idx = h * p.out_sb + static_cast<long long>(m) * p.out_sm + n;
+      float f = __int2float_rn(v[j]);
+      if (!p.raw_f32) f = __fmul_rn(__fmul_rn(f, p.a_scale[h * p.as_sb + m]), ws);
+      store_elem(p.out, p.out_dtype, idx, f);
+      if (p.acc_out) p.acc_out[idx] = v[j];
+    }
+  }
+}
+
+template <int TN, bool kUnsigned>
+__global__ void __launch_bounds__(kThreads, 1)
+    w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+                     const Params p) {
+  constexpr uint32_t kATileBytes = TN * kBlockK;
+  constexpr uint32_t kStageBytes = kWTileBytes + kATileBytes;
+  constexpr uint32_t kTmemCols = TN < 32 ? 32 : TN;
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[kMaxStages];
+  __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+  __shared__ __align__(8) uint64_t tfull_bar, tempty_bar, drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag;
+  __shared__ int sh_issued, sh_consumed, sh_is_last;
+  volatile int* abort_ptr = &abort_flag;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_w = smem;
+  uint8_t* smem_a = smem + p.stages * kWTileBytes;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int S = p.stages;
+  const int KB = p.kb_per_tile;
+  const long long g0 = p.sk.start(blockIdx.x);
+  const long long g1 = p.sk.start(blockIdx.x + 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&tfull_bar, 1);
+    mbar_init(&tempty_bar, 4);
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    sh_issued = 0;
+    sh_consumed = 0;
+    sh_is_last = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_w);
+    prefetch_tmap(&tmap_a);
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(&tmem_base_sh, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_d = tmem_base_sh;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_a = policy_evict_last();
+      const long long nmine = g1 - g0;
+      const int pro = static_cast<int>(nmine < S ? nmine : S);
+      for (int j = 0; j < pro; ++j) {
+        const long long g = g0 + j;
+        const long long tile = g / KB;
+        const int kb = static_cast<int>(g % KB);
+        int h, nt, mt;
+        decode_tile(p, tile, h, nt, mt);
+        mbar_arrive_expect_tx(&full_bar[j], kStageBytes);
+        tma_load_3d(smem_w + j * kWTileBytes, &tmap_w, &full_bar[j], kb * kBlockK, nt * kBlockN, h, pol_w);
+      }
+      // Activations and scales are produced by the preceding kernel.
+      pdl_wait_primary();
+      for (int j = 0; j < pro; ++j) {
+        const long long g = g0 + j;
+        const long long tile = g / KB;
+        const int kb = static_cast<int>(g % KB);
+        int h, nt, mt;
+        decode_tile(p, tile, h, nt, mt);
+        tma_load_3d(smem_a + j * kATileBytes, &tmap_a, &full_bar[j], kb * kBlockK, mt * TN, h, pol_a);
+      }
+      int issued = pro;
+      int stage = pro % S;
+      uint32_t phase = (pro == S) ? 1u : 0u;
+      for (long long g = g0 + pro; g < g1; ++g) {
+        if (*abort_ptr || !mbar_wait(&empty_bar[stage], phase ^ 1u, abort_ptr, p.status)) break;
+        const long long tile = g / KB;
+        const int kb = static_cast<int>(g % KB);
+        int h, nt, mt;
+        decode_tile(p, tile, h, nt, mt);
+        mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+        tma_load_3d(smem_w + stage * kWTileBytes, &tmap_w, &full_bar[stage], kb * kBlockK, nt * kBlockN, h, pol_w);
+        tma_load_3d(smem_a + stage * kATileBytes, &tmap_a, &full_bar[stage], kb * kBlockK, mt * TN, h, pol_a);
+        ++issued;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      sh_issued = issued;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = kUnsigned ? idesc_u8_s32(kBlockN, TN) : idesc_i8_s32(kBlockN, TN);
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      int consumed = 0;
+      bool ok = true;
+      long long g = g0;
+      while (g < g1 && ok) {
+        const long long tile = g / KB;
+        const long long seg_end = (tile + 1) * KB < g1 ? (tile + 1) * KB : g1;
+        if (!mbar_wait(&tempty_bar, acc_phase ^ 1u, abort_ptr, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        bool first = true;
+        for (; g < seg_end; ++g) {
+          if (*abort_ptr || !mbar_wait(&full_bar[stage], phase, abort_ptr, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t wa = smem_u32(smem_w + stage * kWTileBytes);
+          const uint32_t aa = smem_u32(smem_a + stage * kATileBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBlockK / 32; ++kk) {
+            mma_i8_ss(tmem_d, smem_desc_sw128(wa + kk * 32), smem_desc_sw128(aa + kk * 32), idesc,
+                      (first && kk == 0) ? 0u : 1u);
+          }
+          first = false;
+          mma_commit(&empty_bar[stage]);
+          ++consumed;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull_bar);
+        acc_phase ^= 1u;
+      }
+      sh_consumed = consumed;
+      // All issued MMAs must finish before TMEM is released.
+      mma_commit(&drain_bar);
+      mbar_wait(&drain_bar, 0, nullptr, p.status);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    // Control flow is uniform across the 128 epilogue threads even after an
+    // aborted wait: work is skipped, but every named barrier is still reached
+    // by all of them, so no thread can be left waiting on a barrier.
+    pdl_wait_primary();
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_addr = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
+    uint32_t acc_phase = 0;
+    long long g = g0;
+    while (g < g1) {
+      const long long tile = g / KB;
+      const int kb0 = static_cast<int>(g - tile * KB);
+      const long long seg_end = (tile + 1) * KB < g1 ? (tile + 1) * KB : g1;
+      const int kb1 = static_cast<int>(seg_end - tile * KB);
+      const bool first_seg = (g == g0);
+      g = seg_end;
+      const bool got = mbar_wait(&tfull_bar, acc_phase, abort_ptr, p.status);
+      acc_phase ^= 1u;
+      const bool live = __all_sync(0xffffffffu, got);
+      tc_fence_after();
+      int h, nt, mt;
+      decode_tile(p, tile, h, nt, mt);
+      const int n = nt * kBlockN + row;
+      const int m0 = mt * TN;
+      if (kb0 == 0 && kb1 == KB) {
+        // Whole tile in this CTA: epilogue straight from TMEM.
+        if (live) {
+#pragma unroll 1
+          for (int c = 0; c < TN / 16; ++c) {
+            uint32_t r[16];
+            __syncwarp();
+            tmem_ld16(lane_addr + c * 16, r);
+            tmem_ld_wait();
+            int32_t v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = static_cast<int32_t>(r[j]);
+            emit_row<TN>(p, h, n, m0, c * 16, v);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar);
+      } else {
+        // Partial tile: write this CTA's slot, then the last contributor reduces.
+        const int slot = blockIdx.x * 2 + (first_seg ? 0 : 1);
+        int32_t* dst = p.partials + static_cast<long long>(slot) * TN * kBlockN;
+        if (live) {
+#pragma unroll 1
+          for (int c = 0; c < TN / 16; ++c) {
+            uint32_t r[16];
+            __syncwarp();
+            tmem_ld16(lane_addr + c * 16, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) dst[(c * 16 + j) * kBlockN + row] = static_cast<int32_t>(r[j]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar);
+        __threadfence();
+        named_bar_sync(1, 128);
+        const int c_first = p.sk.owner(tile * KB);
+        const int c_last = p.sk.owner((tile + 1) * KB - 1);
+        if (threadIdx.x == 64) {
+          int last = 0;
+          if (!*abort_ptr) {  // an aborted CTA never publishes an incomplete slot
+            const int prev = atomicAdd(&p.counters[c_first], 1);
+            last = (prev == c_last - c_first) ? 1 : 0;
+          }
+          sh_is_last = last;
+        }
+        named_bar_sync(1, 128);
+        if (sh_is_last) {
+          __threadfence();
+#pragma unroll 1
+          for (int c = 0; c < TN / 16; ++c) {
+            int32_t v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0;
+            for (int cc = c_first; cc <= c_last; ++cc) {
+              const int sl = cc * 2 + p.sk.kind(cc, tile);
+              const int32_t* src = p.partials + static_cast<long long>(sl) * TN * kBlockN;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] += __ldcg(src + (c * 16 + j) * kBlockN + row);
+            }
+            emit_row<TN>(p, h, n, m0, c * 16, v);
+          }
+          named_bar_sync(1, 128);
+          if (threadIdx.x == 64) p.counters[c_first] = 0;
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && abort_flag) {
+    // Loads issued but never consumed must land before the CTA exits.
+    for (int j = sh_consumed; j < sh_issued; ++j) mbar_wait(&full_bar[j % S], (j / S) & 1, nullptr, p.status);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_d, kTmemCols);
+  }
+}
+
+template <int TN, bool kUnsigned>
+int launch_tn(const W8A8Launch& L, cudaStream_t stream, int grid, int stages, const Params& prm) {
+  CUtensorMap tw, ta;
+  int st = encode_tmap_3d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.w, static_cast<uint64_t>(L.K),
+                          static_cast<uint64_t>(L.N), static_cast<uint64_t>(L.batch), L.w_sn, L.w_sb, kBlockK,
+                          kBlockN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != CB_OK) return st;
+  st = encode_tmap_3d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.aq, static_cast<uint64_t>(L.K),
+                      static_cast<uint64_t>(L.M), static_cast<uint64_t>(L.batch), L.aq_sm, L.aq_sb, kBlockK, TN,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != CB_OK) return st;
+  const size_t smem = static_cast<size_t>(stages) * (kWTileBytes + TN * kBlockK) + 1024;
+  static thread_local int configured_dev = -1;
+  static thread_local size_t configured_smem = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev || configured_smem < smem) {
+    cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_kernel<TN, kUnsigned>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return CB_ERR_CUDA;
+    configured_dev = dev;
+    configured_smem = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, w8a8_gemm_kernel<TN, kUnsigned>, tw, ta, prm));
+}
+
+template <bool kUnsigned>
+int dispatch_tn(const W8A8Launch& L, cudaStream_t stream, int TN, int grid, int stages, const Params& p) {
+  switch (TN) {
+    case 16:
+      return launch_tn<16, kUnsigned>(L, stream, grid, stages, p);
+    case 32:
+      return launch_tn<32, kUnsigned>(L, stream, grid, stages, p);
+    case 64:
+      return launch_tn<64, kUnsigned>(L, stream, grid, stages, p);
+    case 128:
+      return launch_tn<128, kUnsigned>(L, stream, grid, stages, p);
+    default:
+      return launch_tn<256, kUnsigned>(L, stream, grid, stages, p);
+  }
+}
+
+}  // namespace
+
+size_t w8a8_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K) {
+  (void)batch;
+  (void)N;
+  (void)K;
+  int sms = sm_count();
+  if (sms <= 0) sms = 148;
+  const int TN = token_tile(M);
+  return workspace_need(sms, static_cast<size_t>(TN) * kBlockN * sizeof(int32_t));
+}
+
+int launch_w8a8(const W8A8Launch& L, cudaStream_t stream) {
+  if (L.batch == 0 || L.M == 0 || L.N == 0) return CB_OK;
+  const int TN = token_tile(L.M);
+  Params p = {};
+  p.M = static_cast<int>(L.M);
+  p.N = static_cast<int>(L.N);
+  p.K = static_cast<int>(L.K);
+  p.H = static_cast<int>(L.batch);
+  p.n_tiles = static_cast<int>((L.N + kBlockN - 1) / kBlockN);
+  p.m_tiles = static_cast<int>((L.M + TN - 1) / TN);
+  p.kb_per_tile = static_cast<int>((L.K + kBlockK - 1) / kBlockK);
+  const long long tiles = static_cast<long long>(p.H) * p.n_tiles * p.m_tiles;
+  const long long total = tiles * p.kb_per_tile;
+  int sms = sm_count();
+  if (sms <= 0) return CB_ERR_CUDA;
+  const int grid = static_cast<int>(total < sms ? total : sms);
+  const size_t need = workspace_need(grid, static_cast<size_t>(TN) * kBlockN * sizeof(int32_t));
+  if (L.workspace == nullptr || L.workspace_bytes < need) return CB_ERR_WORKSPACE;
+  // Ring depth: as many stages as ~200 KiB of shared memory holds.
+  const size_t stage_bytes = kWTileBytes + static_cast<size_t>(TN) * kBlockK;
+  int stages = static_cast<int>((200u * 1024u) / stage_bytes);
+  if (stages > kMaxStages) stages = kMaxStages;
+  if (stages < 2) stages = 2;
+  p.stages = stages;
+  p.sk.total = total;
+  p.sk.grid = grid;
+  p.sk.kb_per_tile = p.kb_per_tile;
+  p.a_scale = L.a_scale;
+  p.as_sb = L.as_sb;
+  p.w_scale = L.w_scale;
+  p.ws_sb = L.ws_sb;
+  p.out = L.out;
+  p.out_dtype = L.out_dtype;
+  p.out_sb = L.out_sb;
+  p.out_sm = L.out_sm;
+  p.acc_out = L.acc_out;
+  p.raw_f32 = L.raw_f32;
+  Workspace ws = carve_workspace(L.workspace, grid);
+  p.partials = static_cast<int32_t*>(ws.partials);
+  p.counters = ws.counters;
+  p.status = ws.status;
+  if (L.unsigned_operands) return dispatch_tn<true>(L, stream, TN, grid, stages, p);
+  return dispatch_tn<false>(L, stream, TN, grid, stages, p);
+}
+
+}  // namespace cb

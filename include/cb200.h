@@ -1,0 +1,191 @@
+/*
+ * cb200.h — C ABI of the B200 (sm_100a) quantized-GEMM library.
+ *
+ * The library implements the quantized-GEMM hot path of the cache-barrier
+ * study (W8A8 per-token x per-channel INT8 GEMM, W4A16 int4 group-dequant GEMM,
+ * batched INT4 BMM, packed W4A4 GEMM) as hand-written CUDA for sm_100a
+ * (TMA + tcgen05 + TMEM). Every entry point:
+ *   - takes plain device pointers, sizes and element strides (no framework types);
+ *   - enqueues its work on the caller's stream and returns without a host sync;
+ *   - allocates no device memory: split-K scratch lives in a caller-owned
+ *     workspace whose size cb_workspace_bytes() reports. A workspace must be
+ *     zero-filled once when it is allocated; the kernels leave it zeroed again;
+ *   - returns a cb_status code and never aborts the process.
+ * A workspace may be used by one stream at a time. Calls that share a workspace
+ * on different streams without ordering race.
+ *
+ * Reference interfaces (paths inside the cache-barrier repository) are cited
+ * beside each entry point.
+ */
+#ifndef CB200_H
+#define CB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define CB_API __attribute__((visibility("default")))
+#else
+#define CB_API
+#endif
+
+/* Same handle as cudaStream_t / CUstream. NULL is the legacy default stream. */
+typedef struct CUstream_st* cb_stream_t;
+
+/* ---- status codes ------------------------------------------------------- */
+enum cb_status {
+  CB_OK = 0,
+  CB_ERR_INVALID_ARG = 1,    /* null pointer where one is required, negative size */
+  CB_ERR_SHAPE = 2,          /* a dimension violates a kernel constraint */
+  CB_ERR_DTYPE = 3,          /* unsupported dtype code or dtype combination */
+  CB_ERR_ALIGNMENT = 4,      /* pointer or row stride not 16-byte aligned (TMA rule) */
+  CB_ERR_STRIDE = 5,         /* innermost dimension not contiguous */
+  CB_ERR_WORKSPACE = 6,      /* workspace missing or smaller than cb_workspace_bytes() */
+  CB_ERR_CUDA = 7,           /* a CUDA runtime/driver call failed */
+  CB_ERR_DEVICE_TIMEOUT = 8, /* a bounded device-side wait expired (see cb_workspace_status) */
+  CB_ERR_UNSUPPORTED = 9,    /* no kernel for this device or layout */
+  CB_ERR_TOO_LARGE = 10      /* size beyond a documented maximum */
+};
+
+/* ---- dtype codes -------------------------------------------------------- */
+enum cb_dtype {
+  CB_DTYPE_F16 = 0,
+  CB_DTYPE_BF16 = 1,
+  CB_DTYPE_F32 = 2,
+  CB_DTYPE_I8 = 3,
+  CB_DTYPE_U8 = 4,
+  CB_DTYPE_I32 = 5
+};
+
+/* ---- operation codes (for cb_workspace_bytes) --------------------------- */
+enum cb_op { CB_OP_W8A8 = 0, CB_OP_W4A16 = 1, CB_OP_W4A4 = 2 };
+
+/* ---- int4 weight layouts ------------------------------------------------ */
+enum cb_w4_layout {
+  /* uint8 [batch, K/2, N]: byte (k/2, n) = q[2i] & 0xF | q[2i+1] << 4, two's
+     complement nibbles. profiling/bench_l2_barrier.py:92-99 (quantize_weights_int4). */
+  CB_W4_REF_U8_KN = 0,
+  /* int32 [batch, K/8, N]: nibble j (bits 4j..4j+3) of word (k/8, n) holds q[8*(k/8)+j]. */
+  CB_W4_I32_K8N = 1,
+  /* Kernel-native tiled layout, uint8 [batch, ceil(N/128), ceil(K/128), 128, 64]:
+     one contiguous 8 KiB tile per (128 rows of N) x (128 of K), zero padded.
+     Row r of a tile is 64 bytes = four 16-byte chunks; chunk j (k = 32j..32j+31)
+     is stored at chunk position j ^ ((r >> 1) & 3). Each 32-bit word holds 8
+     consecutive k as nibbles in the order k0,k2,k4,k6,k1,k3,k5,k7. */
+  CB_W4_NATIVE = 2
+};
+
+/* Human-readable name of a status code (static string). */
+CB_API const char* cb_status_str(int status);
+
+/* Library ABI version: major * 10000 + minor * 100 + patch. */
+CB_API int cb_version(void);
+
+/* Number of SMs the kernels size their grids for on the current device
+   (0 when no device is visible). */
+CB_API int cb_device_sm_count(void);
+
+/* Workspace bytes needed by op for a GEMM of `batch` x [M x K] x [K x N]. */
+CB_API size_t cb_workspace_bytes(int op, int64_t batch, int64_t M, int64_t N, int64_t K);
+
+/* Copies the workspace status word to *device_status after synchronizing the
+   stream. Returns CB_ERR_DEVICE_TIMEOUT if a kernel recorded an expired wait
+   (and then clears the word), CB_OK otherwise. */
+CB_API int cb_workspace_status(void* workspace, int* device_status, cb_stream_t stream);
+
+/* ---- activation quantization ------------------------------------------- */
+/* Per-(batch, row) symmetric int8: scale = max(amax/127, 1e-8),
+   q = trunc(a/scale + 0.5*sign(a)) (round half away from zero), IEEE-rounded
+   fp32 division. Replaces _quant_act_kernel / quantize_acts_w8
+   (profiling/w8a8/w8a8_bmm.py:21-41, 92-106).
+   a: [batch, M, K] f16 or bf16, K contiguous, strides in elements.
+   q: [batch, M, K] int8, K contiguous. scale: fp32, scale[b * scale_stride_b + m]. */
+CB_API int cb_quant_act_i8(const void* a, int a_dtype, int64_t batch, int64_t M, int64_t K, int64_t a_stride_b,
+                    int64_t a_stride_m, int8_t* q, int64_t q_stride_b, int64_t q_stride_m, float* scale,
+                    int64_t scale_stride_b, cb_stream_t stream);
+
+/* ---- W8A8 INT8 GEMM ----------------------------------------------------- */
+/* out[b, m, n] = cvt( (float)acc[b, m, n] * a_scale[b, m] * w_scale[b, n] ),
+   acc = sum_k aq[b, m, k] * w[b, n, k] in int32 (bit exact).
+   Replaces _w8a8_bmm_kernel / w8a8_bmm (profiling/w8a8/w8a8_bmm.py:44-81, 118-140).
+   aq: int8 [batch, M, K], K contiguous.
+   w : int8 [batch, N, K], K contiguous (K-major; the reference's [batch, K, N]
+       weight viewed transposed — see cb_repack_w8_kmajor).
+   out: [batch, M, N] f16 / bf16 / f32, N contiguous.
+   acc_out: optional int32 [batch, M, N] (same strides as out) receiving the raw
+       accumulators; NULL to skip.
+   strides (elements): {aq_b, aq_m, w_b, w_n, out_b, out_m, a_scale_b, w_scale_b}.
+   Constraints: K % 16 == 0, 16-byte aligned aq/w and row strides. */
+CB_API int cb_w8a8_gemm(const int8_t* aq, const float* a_scale, const int8_t* w, const float* w_scale, void* out,
+                 int out_dtype, int32_t* acc_out, int64_t batch, int64_t M, int64_t N, int64_t K,
+                 const int64_t* strides, void* workspace, size_t workspace_bytes, cb_stream_t stream);
+
+/* Dynamic per-token activation quantization followed by the W8A8 GEMM, two
+   launches chained with programmatic dependent launch so the GEMM's weight
+   stream starts while the quantization runs. Replaces w8a8_bmm_full
+   (profiling/w8a8/w8a8_bmm.py:143-149). q_buf / s_buf are caller buffers that
+   receive the quantized activations (int8 [batch, M, K] contiguous) and scales
+   (fp32 [batch * M]), as the reference's `bufs`.
+   strides (elements): {a_b, a_m, w_b, w_n, out_b, out_m, w_scale_b}. */
+CB_API int cb_w8a8_gemm_dynamic(const void* a, int a_dtype, int8_t* q_buf, float* s_buf, const int8_t* w,
+                         const float* w_scale, void* out, int out_dtype, int64_t batch, int64_t M, int64_t N,
+                         int64_t K, const int64_t* strides, void* workspace, size_t workspace_bytes,
+                         cb_stream_t stream);
+
+/* ---- W4A16 int4 group-dequant GEMM / batched INT4 BMM -------------------- */
+/* out[b, m, n] = sum_k a[b, m, k] * (q[b, k, n] * s[b, k / group_size, n]).
+   Replaces kernel_batched_w4a16_simple / batched_int4_gemm
+   (profiling/bench_l2_barrier.py:36-85, 102-125; profiling/int4_batched_gemm.py:130-265;
+   profiling/int4_batched_gemm_v2.py:140-260) and generalises the per-channel
+   scale (group_size == K) to group_size 128 (or any multiple of 128).
+   a: [batch, M, K] f16 or bf16 (K contiguous); the MMA runs in a's dtype.
+   w_native: CB_W4_NATIVE layout (see cb_repack_w4).
+   scales: [batch, ceil(K/group_size), N] f16 / bf16 / f32, N contiguous.
+   out: [batch, M, N] f16 / bf16 / f32, N contiguous.
+   strides (elements): {a_b, a_m, s_b, s_g, out_b, out_m}.
+   Constraints: K % 8 == 0; group_size % 128 == 0 or group_size >= K. */
+CB_API int cb_w4a16_gemm(const void* a, int a_dtype, const uint8_t* w_native, const void* scales, int scale_dtype,
+                  int64_t group_size, void* out, int out_dtype, int64_t batch, int64_t M, int64_t N, int64_t K,
+                  const int64_t* strides, void* workspace, size_t workspace_bytes, cb_stream_t stream);
+
+/* ---- W4A4 packed int4 GEMM ---------------------------------------------- */
+/* Nibble interpretation for cb_w4a4_gemm. */
+enum cb_w4a4_mode {
+  /* two's complement int4 in [-8, 7]: the function's documented contract
+     (kernels/triton_gemm.py:407-411) and its own check (:492-520). */
+  CB_W4A4_SIGNED = 0,
+  /* what the reference kernel computes: `v - 16` on a uint8 tensor for v >= 8
+     (kernels/triton_gemm.py:164-167) wraps to 240..255. */
+  CB_W4A4_REF_UINT8_WRAP = 1
+};
+/* C[m, n] = sum_k A[m, k] * B[k, n] as fp32 (exact integer sums, one rounding).
+   Replaces triton_gemm_packed_int4 (kernels/triton_gemm.py:395-485).
+   a_packed: uint8 [M, K/2] (byte (m, i) holds k = 2i low, 2i+1 high), row stride lda.
+   b_packed: uint8 [K/2, N], row stride ldb. c: fp32 [M, N], row stride ldc.
+   The workspace also holds the unpacked 8-bit operands. K % 32 == 0. */
+CB_API int cb_w4a4_gemm(const uint8_t* a_packed, const uint8_t* b_packed, float* c, int64_t M, int64_t N, int64_t K,
+                        int64_t lda, int64_t ldb, int64_t ldc, int nibble_mode, void* workspace,
+                        size_t workspace_bytes, cb_stream_t stream);
+
+/* ---- weight preparation (offline, device-side) -------------------------- */
+/* Repack int4 weights from CB_W4_REF_U8_KN or CB_W4_I32_K8N into CB_W4_NATIVE.
+   src strides are the dense strides of the source layout; dst must hold
+   cb_w4_native_bytes(batch, K, N) bytes. */
+CB_API int cb_repack_w4(const void* src, int src_layout, uint8_t* dst_native, int64_t batch, int64_t K, int64_t N,
+                 cb_stream_t stream);
+CB_API size_t cb_w4_native_bytes(int64_t batch, int64_t K, int64_t N);
+
+/* Transpose int8 weights [batch, K, N] (N contiguous, the reference layout of
+   quantize_weights_w8, profiling/w8a8/w8a8_bmm.py:84-89) into [batch, N, K]. */
+CB_API int cb_repack_w8_kmajor(const int8_t* src_kn, int8_t* dst_nk, int64_t batch, int64_t K, int64_t N,
+                        cb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CB200_H */

@@ -1,0 +1,291 @@
+"""CPU oracle for the quantized-GEMM hot path — TEST INFRASTRUCTURE ONLY.
+
+This module restates the cache-barrier reference arithmetic in numpy. It is the
+checker for the CUDA kernels: only ``tests/``, ``__graft_entry__.smoke()`` and the
+CPU-baseline leg of ``bench.py`` may import it. No product code path calls it.
+
+Pinning: every function below is checked in ``tests/test_oracle_golden.py``
+against golden vectors produced by the reference's own code (its Triton kernels
+run under Triton's CPU interpreter and its PyTorch quantizers), committed in
+``tests/golden/`` together with the script that generated them
+(``tests/golden/make_golden.py``). The group-size-128 W4A16 extension has no
+reference implementation; its restatement follows the reference's explicit
+dequant (profiling/gate/bench_capacity_gate.py:235-244) with the scale indexed
+per group, and that case alone is "parity unpinned" beyond the per-channel
+pinning.
+
+Exactness: integer GEMMs are computed as float64 matmuls of int8-valued arrays,
+which is exact while every partial sum stays below 2**53 (|sum| <= 127*127*K for
+K < 5e11).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+# ---------------------------------------------------------------------------
+# bf16 helpers (numpy has no bfloat16): values are carried as uint16 bit patterns.
+# ---------------------------------------------------------------------------
+
+
+def f32_to_bf16_bits(x) -> np.ndarray:
+    """Round fp32 to bf16, round-to-nearest-even, NaN kept quiet."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32)
+    rounding = ((u >> 16) & 1) + np.uint32(0x7FFF)
+    out = ((u + rounding) >> 16).astype(np.uint16)
+    nan = np.isnan(x)
+    if nan.any():
+        out = np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), out)
+    return out
+
+
+def bf16_bits_to_f32(b) -> np.ndarray:
+    b = np.ascontiguousarray(b, dtype=np.uint16)
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def round_to(x, dtype: str) -> np.ndarray:
+    """fp32 -> output dtype: 'f16' (np.float16), 'bf16' (uint16 bits) or 'f32'."""
+    x = np.asarray(x, dtype=np.float32)
+    if dtype == "f16":
+        return x.astype(np.float16)
+    if dtype == "bf16":
+        return f32_to_bf16_bits(x)
+    if dtype == "f32":
+        return x
+    raise ValueError(dtype)
+
+
+def as_f32(x, dtype: str) -> np.ndarray:
+    """Inverse view of round_to: stored values -> fp32."""
+    if dtype == "bf16":
+        return bf16_bits_to_f32(x)
+    return np.asarray(x, dtype=np.float32)
+
+
+# ---------------------------------------------------------------------------
+# Weight quantizers
+# ---------------------------------------------------------------------------
+
+
+def quantize_weights_int4(W: np.ndarray):
+    """Per-output-channel symmetric int4, restating quantize_weights_int4
+    (profiling/bench_l2_barrier.py:92-99) for fp16 W of shape [..., K, N].
+
+    fp16 arithmetic as torch performs it (each op computed in fp32 and rounded to
+    fp16): amax over K, clamp(min=1e-8), /7, W/scale, round half to even, clamp
+    to [-8, 7]. Returns (q int8 [..., K, N], scale fp16 [..., N]).
+    """
+    W = np.asarray(W, dtype=np.float16)
+    w_max = np.abs(W).max(axis=-2, keepdims=True)
+    w_max = np.where(w_max.astype(np.float32) < np.float32(1e-8), np.float16(1e-8), w_max).astype(np.float16)
+    scale = (w_max.astype(np.float32) / np.float32(7.0)).astype(np.float16)
+    ratio = (W.astype(np.float32) / scale.astype(np.float32)).astype(np.float16)
+    q = np.clip(np.rint(ratio.astype(np.float32)), -8, 7).astype(np.int8)
+    return q, scale[..., 0, :]
+
+
+def quantize_weights_w8(w: np.ndarray):
+    """Per-(H, N) symmetric int8, restating quantize_weights_w8
+    (profiling/w8a8/w8a8_bmm.py:84-89): s = amax_K(|w|)/127 clamped at 1e-8,
+    q = round_half_even(w / s) clamped to [-127, 127], all in fp32."""
+    wf = np.asarray(w, dtype=np.float32)
+    s = (np.abs(wf).max(axis=-2) / np.float32(127.0)).astype(np.float32)
+    s = np.maximum(s, np.float32(1e-8))
+    q = np.clip(np.rint(wf / s[..., None, :]), -127, 127).astype(np.int8)
+    return q, s
+
+
+# ---------------------------------------------------------------------------
+# W8A8
+# ---------------------------------------------------------------------------
+
+
+def quant_act_i8(a_f32: np.ndarray):
+    """Per-row symmetric int8 of a [..., K] (fp32 view of f16/bf16 input),
+    restating _quant_act_kernel (profiling/w8a8/w8a8_bmm.py:35-41):
+    scale = max(amax/127, 1e-8); q = trunc(a/scale + 0.5*sign(a)) with
+    sign(0) = +1, IEEE-rounded fp32 division and addition.
+    Returns (q int8 [..., K], scale fp32 [...])."""
+    a = np.asarray(a_f32, dtype=np.float32)
+    amax = np.abs(a).max(axis=-1)
+    scale = np.maximum(amax / np.float32(127.0), np.float32(1e-8)).astype(np.float32)
+    half = np.where(a >= 0, np.float32(0.5), np.float32(-0.5))
+    y = (a / scale[..., None]).astype(np.float32) + half
+    q = np.trunc(y.astype(np.float32)).astype(np.int8)
+    return q, scale
+
+
+def gemm_i8_i32(aq: np.ndarray, wq_kn: np.ndarray) -> np.ndarray:
+    """Exact int32 accumulators sum_k aq[..., m, k] * wq[..., k, n]."""
+    acc = np.matmul(aq.astype(np.float64), wq_kn.astype(np.float64))
+    assert np.abs(acc).max(initial=0) < 2.0**31
+    return acc.astype(np.int32)
+
+
+def w8a8_epilogue(acc: np.ndarray, a_scale: np.ndarray, w_scale: np.ndarray, out_dtype: str) -> np.ndarray:
+    """((float)acc * a_scale[m]) * w_scale[n], then cast (profiling/w8a8/w8a8_bmm.py:78-81).
+    acc [B, M, N] int32, a_scale [B, M] fp32, w_scale [B, N] fp32."""
+    f = acc.astype(np.float32)
+    f = (f * a_scale.astype(np.float32)[..., :, None]).astype(np.float32)
+    f = (f * w_scale.astype(np.float32)[..., None, :]).astype(np.float32)
+    return round_to(f, out_dtype)
+
+
+def w8a8_dynamic(a_f32: np.ndarray, wq_kn: np.ndarray, w_scale: np.ndarray, out_dtype: str):
+    """Act quant + int GEMM + epilogue (w8a8_bmm_full, profiling/w8a8/w8a8_bmm.py:143-149).
+    Returns (out, q, a_scale, acc)."""
+    q, s = quant_act_i8(a_f32)
+    acc = gemm_i8_i32(q, wq_kn)
+    return w8a8_epilogue(acc, s, w_scale, out_dtype), q, s, acc
+
+
+# ---------------------------------------------------------------------------
+# W4A16
+# ---------------------------------------------------------------------------
+
+
+def dequant_w4(q: np.ndarray, scales: np.ndarray, group_size: int) -> np.ndarray:
+    """w[k, n] = q[k, n] * s[k // group_size, n] in fp32 (exact: 4-bit x <=24-bit).
+    q [..., K, N] int, scales [..., G, N] float."""
+    K = q.shape[-2]
+    gidx = np.arange(K) // group_size
+    s = np.asarray(scales, dtype=np.float32)[..., gidx, :]
+    return q.astype(np.float32) * s
+
+
+def w4a16_gemm(a_f32: np.ndarray, q: np.ndarray, scales: np.ndarray, group_size: int) -> np.ndarray:
+    """fp32 result of a @ dequant(q, scales), accumulated in float64 (then fp32).
+    Explicit-dequant restatement of profiling/gate/bench_capacity_gate.py:235-244."""
+    w = dequant_w4(q, scales, group_size).astype(np.float64)
+    return np.matmul(np.asarray(a_f32, dtype=np.float64), w).astype(np.float32)
+
+
+def w4a16_per_channel(a_f32: np.ndarray, q: np.ndarray, scale_n: np.ndarray) -> np.ndarray:
+    """kernel_batched_w4a16_simple's order: scale applied once to the accumulator
+    (profiling/bench_l2_barrier.py:78-82). scale_n [..., N]."""
+    acc = np.matmul(np.asarray(a_f32, dtype=np.float64), q.astype(np.float64))
+    return (acc.astype(np.float32) * np.asarray(scale_n, dtype=np.float32)[..., None, :]).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# W4A4
+# ---------------------------------------------------------------------------
+
+
+def unpack_rows_i4(packed: np.ndarray, wrap: bool = False) -> np.ndarray:
+    """uint8 [M, K/2] (k = 2i low nibble, 2i+1 high) -> int16 [M, K]
+    (kernels/triton_gemm.py:159-167). Nibbles >= 8 become v - 16 (signed int4), or,
+    with ``wrap``, (v - 16) mod 256 = 240..255: the reference kernel subtracts 16
+    on a uint8 tensor, which wraps."""
+    lo = (packed & 0xF).astype(np.int16)
+    hi = (packed >> 4).astype(np.int16)
+    off = 240 if wrap else -16
+    lo = np.where(lo >= 8, lo + off, lo)
+    hi = np.where(hi >= 8, hi + off, hi)
+    out = np.empty(packed.shape[:-1] + (packed.shape[-1] * 2,), dtype=np.int16)
+    out[..., 0::2] = lo
+    out[..., 1::2] = hi
+    return out
+
+
+def w4a4_gemm(a_packed: np.ndarray, b_packed: np.ndarray, wrap: bool = False) -> np.ndarray:
+    """fp32 C = A @ B over unpacked nibbles; exact integer sums, rounded once to fp32
+    (kernels/triton_gemm.py:159-176). ``wrap`` selects the reference kernel's
+    uint8-wrap reading of negative nibbles (see unpack_rows_i4)."""
+    a = unpack_rows_i4(a_packed, wrap)
+    b = unpack_rows_i4(np.ascontiguousarray(b_packed.T), wrap).T  # B [K/2, N] packs k along rows
+    return np.matmul(a.astype(np.float64), b.astype(np.float64)).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# int4 layout codecs
+# ---------------------------------------------------------------------------
+
+
+def pack_u8_kn(q: np.ndarray) -> np.ndarray:
+    """int [..., K, N] in [-8, 7] -> uint8 [..., K/2, N], even k in the low nibble
+    (profiling/bench_l2_barrier.py:96-98)."""
+    q = np.asarray(q).astype(np.int16)
+    even = (q[..., 0::2, :] & 0xF).astype(np.uint8)
+    odd = (q[..., 1::2, :] & 0xF).astype(np.uint8)
+    return (even | (odd << 4)).astype(np.uint8)
+
+
+def unpack_u8_kn(p: np.ndarray) -> np.ndarray:
+    lo = (p & 0xF).astype(np.int16)
+    hi = (p >> 4).astype(np.int16)
+    lo = np.where(lo >= 8, lo - 16, lo)
+    hi = np.where(hi >= 8, hi - 16, hi)
+    K2 = p.shape[-2]
+    out = np.empty(p.shape[:-2] + (2 * K2, p.shape[-1]), dtype=np.int8)
+    out[..., 0::2, :] = lo
+    out[..., 1::2, :] = hi
+    return out
+
+
+def pack_i32_k8n(q: np.ndarray) -> np.ndarray:
+    """int [..., K, N] -> int32 [..., K/8, N]; nibble j of word (k/8, n) = q[8*(k/8)+j]."""
+    q = np.asarray(q).astype(np.int64) & 0xF
+    K = q.shape[-2]
+    w = np.zeros(q.shape[:-2] + (K // 8, q.shape[-1]), dtype=np.uint32)
+    for j in range(8):
+        w |= (q[..., j::8, :].astype(np.uint32) << np.uint32(4 * j))
+    return w.view(np.int32)
+
+
+def unpack_i32_k8n(w: np.ndarray) -> np.ndarray:
+    u = np.asarray(w).view(np.uint32)
+    K8 = u.shape[-2]
+    out = np.empty(u.shape[:-2] + (K8 * 8, u.shape[-1]), dtype=np.int8)
+    for j in range(8):
+        v = ((u >> np.uint32(4 * j)) & 0xF).astype(np.int16)
+        out[..., j::8, :] = np.where(v >= 8, v - 16, v)
+    return out
+
+
+_NATIVE_POS = np.array([0, 4, 1, 5, 2, 6, 3, 7])  # nibble position of k0..k7 (order k0,k2,k4,k6,k1,k3,k5,k7)
+
+
+def pack_native(q: np.ndarray) -> np.ndarray:
+    """int [B, K, N] -> flat uint8 native tiled layout (include/cb200.h CB_W4_NATIVE)."""
+    q = np.asarray(q)
+    if q.ndim == 2:
+        q = q[None]
+    B, K, N = q.shape
+    nt, kt = -(-N // 128), -(-K // 128)
+    qp = np.zeros((B, kt * 128, nt * 128), dtype=np.int64)
+    qp[:, :K, :N] = q
+    nib = (qp & 0xF).astype(np.uint32)
+    # [B, kt, 128(k), nt, 128(r)] -> [B, nt, kt, r, k]
+    t = nib.reshape(B, kt, 128, nt, 128).transpose(0, 3, 1, 4, 2)
+    # k = chunk*32 + word*8 + j
+    t = t.reshape(B, nt, kt, 128, 4, 4, 8)
+    words = np.zeros(t.shape[:-1], dtype=np.uint32)
+    for j in range(8):
+        words |= t[..., j] << np.uint32(4 * _NATIVE_POS[j])
+    # stored chunk position c' = c ^ ((r >> 1) & 3)
+    r = np.arange(128)
+    out = np.empty_like(words)
+    for c in range(4):
+        pos = c ^ ((r >> 1) & 3)
+        out[:, :, :, r, pos, :] = words[:, :, :, r, c, :]
+    return out.reshape(-1).view(np.uint8)
+
+
+def unpack_native(buf: np.ndarray, B: int, K: int, N: int) -> np.ndarray:
+    nt, kt = -(-N // 128), -(-K // 128)
+    words = np.asarray(buf).view(np.uint32).reshape(B, nt, kt, 128, 4, 4)
+    r = np.arange(128)
+    logical = np.empty_like(words)
+    for c in range(4):
+        pos = c ^ ((r >> 1) & 3)
+        logical[:, :, :, r, c, :] = words[:, :, :, r, pos, :]
+    vals = np.empty(logical.shape + (8,), dtype=np.int16)
+    for j in range(8):
+        v = ((logical >> np.uint32(4 * _NATIVE_POS[j])) & 0xF).astype(np.int16)
+        vals[..., j] = np.where(v >= 8, v - 16, v)
+    # [B, nt, kt, r, chunk, word, j] -> [B, kt*128, nt*128]
+    vals = vals.reshape(B, nt, kt, 128, 128).transpose(0, 2, 4, 1, 3).reshape(B, kt * 128, nt * 128)
+    return vals[:, :K, :N].astype(np.int8)

@@ -1,0 +1,105 @@
+"""The oracle against golden vectors made by the reference's own code
+(tests/golden/make_golden.py runs its Triton kernels under the interpreter)."""
+
+import numpy as np
+import pytest
+
+from oracle import quant_oracle as O
+
+W4A16_FIXTURES = ["w4a16_h2_t3_k256_n192.npz", "w4a16_h4_t1_k128_n256.npz", "w4a16_h2_t17_k512_n128.npz"]
+W8A8_FIXTURES = ["w8a8_h2_m5_k256_n192.npz", "w8a8_h1_m1_k512_n256.npz", "w8a8_h2_m33_k128_n64_bf16.npz"]
+
+
+def _acts(d):
+    if bool(d["a_is_bf16_bits"]):
+        return O.bf16_bits_to_f32(d["a"].view(np.uint16))
+    return d["a"].astype(np.float32)
+
+
+def test_quantize_weights_int4_bit_exact(golden):
+    d = golden("w4a16_h2_t3_k256_n192.npz")
+    q, s = O.quantize_weights_int4(d["w"])
+    assert np.array_equal(O.pack_u8_kn(q), d["packed"])
+    assert np.array_equal(s.view(np.uint16), d["scales"].view(np.uint16))
+
+
+@pytest.mark.parametrize("name", W4A16_FIXTURES)
+@pytest.mark.parametrize("kernel", ["c_simple", "c_v1", "c_v3"])
+def test_w4a16_per_channel_matches_reference_kernels(golden, name, kernel):
+    d = golden(name)
+    q = O.unpack_u8_kn(d["packed"])
+    ref = O.w4a16_per_channel(d["x"].astype(np.float32), q, d["scales"].astype(np.float32))
+    out = O.round_to(ref, "f16").astype(np.float32)
+    got = d[kernel].astype(np.float32)
+    # fp32 accumulation order is the only difference: at most 1 fp16 ulp here.
+    assert np.abs(out - got).max() <= 2.0 ** -10 * np.abs(got).max()
+    assert (out.view(np.uint32) == got.view(np.uint32)).mean() > 0.999
+
+
+@pytest.mark.parametrize("name", W8A8_FIXTURES)
+def test_w8a8_matches_reference_bit_exact(golden, name):
+    d = golden(name)
+    q, s = O.quant_act_i8(_acts(d))
+    assert np.array_equal(q, d["q"])
+    assert np.array_equal(s.reshape(-1).view(np.uint32), d["s"].view(np.uint32))
+    if "w" in d:
+        wq, ws = O.quantize_weights_w8(d["w"])
+        assert np.array_equal(wq, d["wq"])
+        assert np.array_equal(ws.view(np.uint32), d["wscale"].view(np.uint32))
+    acc = O.gemm_i8_i32(d["q"], d["wq"])
+    out = O.w8a8_epilogue(acc, d["s"].reshape(acc.shape[0], -1), d["wscale"], "f16")
+    assert np.array_equal(out.view(np.uint16), d["out"].view(np.uint16))
+
+
+def test_act_quant_ties_and_zero_rows(golden):
+    d = golden("act_quant_ties.npz")
+    q, s = O.quant_act_i8(d["a"].astype(np.float32))
+    assert np.array_equal(q, d["q"])
+    assert np.array_equal(s.reshape(-1).view(np.uint32), d["s"].view(np.uint32))
+    # half away from zero on exact .5 ties
+    assert list(q[0, 0, :5]) == [127, 3, -3, 1, -1]
+
+
+def test_w4a4_reference_wrap_and_signed(golden):
+    d = golden("w4a4_m5_k256_n96.npz")
+    # the reference kernel's uint8 arithmetic: reproduced bit for bit
+    assert np.array_equal(O.w4a4_gemm(d["a_packed"], d["b_packed"], wrap=True), d["c"])
+    # the signed reading differs wherever a negative nibble is present
+    signed = O.w4a4_gemm(d["a_packed"], d["b_packed"], wrap=False)
+    assert not np.array_equal(signed, d["c"])
+    assert np.abs(signed).max() <= 64 * 256
+
+
+@pytest.mark.parametrize("B,K,N", [(1, 128, 128), (2, 256, 192), (1, 384, 130), (3, 136, 72), (1, 8, 8)])
+def test_layout_codecs_round_trip(B, K, N):
+    rng = np.random.default_rng(K * N + B)
+    q = rng.integers(-8, 8, size=(B, K, N)).astype(np.int8)
+    assert np.array_equal(O.unpack_u8_kn(O.pack_u8_kn(q)), q)
+    assert np.array_equal(O.unpack_i32_k8n(O.pack_i32_k8n(q)), q)
+    nat = O.pack_native(q)
+    assert nat.nbytes == B * (-(-N // 128)) * (-(-K // 128)) * 8192
+    assert np.array_equal(O.unpack_native(nat, B, K, N), q)
+
+
+def test_native_layout_word_order():
+    # one tile, row 0: k = 0..7 -> nibble order k0,k2,k4,k6,k1,k3,k5,k7 in word 0
+    q = np.zeros((1, 128, 128), dtype=np.int8)
+    q[0, :8, 0] = [1, 2, 3, 4, 5, 6, -7, -8]
+    words = O.pack_native(q).view(np.uint32)
+    expect = 0
+    for pos, k in enumerate([0, 2, 4, 6, 1, 3, 5, 7]):
+        expect |= (int(q[0, k, 0]) & 0xF) << (4 * pos)
+    assert words[0] == expect
+    # row 2 chunk 0 is stored at chunk position (2 >> 1) & 3 = 1
+    q2 = np.zeros((1, 128, 128), dtype=np.int8)
+    q2[0, 0, 2] = 5
+    w2 = O.pack_native(q2).view(np.uint32).reshape(128, 16)
+    assert w2[2, 4] == 5 and w2[2, 0] == 0
+
+
+def test_bf16_rounding_helper():
+    x = np.array([1.0, 1.00390625, 1.005859375, -2.5, 3.0e38, 1e-30], dtype=np.float32)
+    b = O.f32_to_bf16_bits(x)
+    assert list(b[:4]) == [0x3F80, 0x3F80, 0x3F81, 0xC020]
+    back = O.bf16_bits_to_f32(b)
+    assert np.all(np.abs(back - x) <= np.abs(x) * 2.0 ** -8)
