@@ -19,12 +19,12 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // SM count of the current device (cached per device); 0 if no device.
 int sm_count();
 
-// Token tile (MMA N) for M tokens: 16, 32, 64, 128 or 256.
-inline int token_tile(int64_t M) {
+// Token tile (MMA N) for M tokens: 16, 32, 64, 128 or (max_tile permitting) 256.
+inline int token_tile(int64_t M, int max_tile = 256) {
   if (M <= 16) return 16;
   if (M <= 32) return 32;
   if (M <= 64) return 64;
-  if (M <= 128) return 128;
+  if (M <= 128 || max_tile <= 128) return 128;
   return 256;
 }
 
@@ -35,16 +35,23 @@ struct Workspace {
   void* partials;
 };
 
+// Workspace layout (fixed, so calls of different shapes that share one
+// workspace agree on it): [status word + padding][kMaxGrid arrival counters]
+// [2 partial slots per CTA].
+constexpr int kMaxGrid = 1024;
+constexpr size_t kWsCounters = kMaxGrid * sizeof(int);
+
 inline size_t workspace_need(int grid, size_t slot_bytes) {
-  return kWsHeader + align_up(static_cast<size_t>(grid) * sizeof(int), 256) + 2 * static_cast<size_t>(grid) * slot_bytes;
+  return kWsHeader + kWsCounters + 2 * static_cast<size_t>(grid) * slot_bytes;
 }
 
 inline Workspace carve_workspace(void* ws, int grid) {
+  (void)grid;
   Workspace w;
   char* base = static_cast<char*>(ws);
   w.status = reinterpret_cast<int*>(base);
   w.counters = reinterpret_cast<int*>(base + kWsHeader);
-  w.partials = base + kWsHeader + align_up(static_cast<size_t>(grid) * sizeof(int), 256);
+  w.partials = base + kWsHeader + kWsCounters;
   return w;
 }
 

@@ -42,6 +42,8 @@ constexpr int kNumABuf = 4;
 constexpr uint32_t kACols = kBlockK / 2;  // 32-bit TMEM columns per A buffer (2 x 16-bit per column)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kDCol = kNumABuf * kACols;  // accumulator starts after the A buffers
+// Largest token tile used: 128 (M > 128 is covered by several 128-token tiles).
+constexpr int kMaxTokenTile = 128;
 
 struct Params {
   int M, N, K, H;
@@ -238,6 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = idesc_f16_f32(kBlockN, TN, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
       uint32_t acc_phase = 0;
       int consumed = 0;
+      int n_tfull = 0;
       bool ok = true;
       long long g = g0;
       while (g < g1 && ok) {
@@ -276,10 +279,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         mma_commit(&tfull_bar);
         acc_phase ^= 1u;
+        ++n_tfull;
       }
       sh_consumed = consumed;
       mma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, nullptr, p.status);
+      // Every commit arrival this thread issued must land before the CTA exits
+      // (an arrive on released shared memory faults): the releases of the last
+      // S stages, of the last use of each TMEM A buffer, and the last
+      // accumulator hand-off.
+      for (int j = consumed > S ? consumed - S : 0; j < consumed; ++j)
+        mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
+      for (int j = consumed > kNumABuf ? consumed - kNumABuf : 0; j < consumed; ++j)
+        mbar_wait(&aempty_bar[j & (kNumABuf - 1)], static_cast<uint32_t>((j >> 2) & 1), nullptr, p.status);
+      if (n_tfull > 0) mbar_wait(&tfull_bar, static_cast<uint32_t>((n_tfull - 1) & 1), nullptr, p.status);
     }
   } else {
     // ---------------- dequant warpgroups (warps 2-5: group 0, 6-9: group 1) ----------------
@@ -481,10 +494,8 @@ int launch_dtype(const W4A16Launch& L, cudaStream_t stream, int TN, int grid, in
       return launch_typed<T, 32>(L, stream, grid, stages, p);
     case 64:
       return launch_typed<T, 64>(L, stream, grid, stages, p);
-    case 128:
-      return launch_typed<T, 128>(L, stream, grid, stages, p);
     default:
-      return launch_typed<T, 256>(L, stream, grid, stages, p);
+      return launch_typed<T, 128>(L, stream, grid, stages, p);
   }
 }
 
@@ -496,11 +507,11 @@ size_t w4a16_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K) {
   (void)K;
   int sms = sm_count();
   if (sms <= 0) sms = 148;
-  return workspace_need(sms, static_cast<size_t>(token_tile(M)) * kBlockN * sizeof(float));
+  return workspace_need(sms, static_cast<size_t>(token_tile(M, kMaxTokenTile)) * kBlockN * sizeof(float));
 }
 
 int launch_w4a16(const W4A16Launch& L, cudaStream_t stream) {
-  const int TN = token_tile(L.M);
+  const int TN = token_tile(L.M, kMaxTokenTile);
   Params p = {};
   p.M = static_cast<int>(L.M);
   p.N = static_cast<int>(L.N);
@@ -513,7 +524,8 @@ int launch_w4a16(const W4A16Launch& L, cudaStream_t stream) {
   const long long total = tiles * p.kb_per_tile;
   const int sms = sm_count();
   if (sms <= 0) return CB_ERR_CUDA;
-  const int grid = static_cast<int>(total < sms ? total : sms);
+  const int max_grid = sms < kMaxGrid ? sms : kMaxGrid;
+  const int grid = static_cast<int>(total < max_grid ? total : max_grid);
   const size_t need = workspace_need(grid, static_cast<size_t>(TN) * kBlockN * sizeof(float));
   if (L.workspace == nullptr || L.workspace_bytes < need) return CB_ERR_WORKSPACE;
   const size_t stage_bytes = kWTileBytes + static_cast<size_t>(TN) * kBlockK * 2;

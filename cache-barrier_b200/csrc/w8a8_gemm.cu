@@ -183,6 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0, acc_phase = 0;
       int consumed = 0;
+      int n_tfull = 0;
       bool ok = true;
       long long g = g0;
       while (g < g1 && ok) {
@@ -218,11 +219,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         mma_commit(&tfull_bar);
         acc_phase ^= 1u;
+        ++n_tfull;
       }
       sh_consumed = consumed;
       // All issued MMAs must finish before TMEM is released.
       mma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, nullptr, p.status);
+      // Every commit arrival this thread issued must land before the CTA exits
+      // (an arrive on released shared memory faults): the releases of the last
+      // S stages and the last accumulator hand-off.
+      for (int j = consumed > S ? consumed - S : 0; j < consumed; ++j)
+        mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
+      if (n_tfull > 0) mbar_wait(&tfull_bar, static_cast<uint32_t>((n_tfull - 1) & 1), nullptr, p.status);
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
@@ -413,7 +421,8 @@ int launch_w8a8(const W8A8Launch& L, cudaStream_t stream) {
   const long long total = tiles * p.kb_per_tile;
   int sms = sm_count();
   if (sms <= 0) return CB_ERR_CUDA;
-  const int grid = static_cast<int>(total < sms ? total : sms);
+  const int max_grid = sms < kMaxGrid ? sms : kMaxGrid;
+  const int grid = static_cast<int>(total < max_grid ? total : max_grid);
   const size_t need = workspace_need(grid, static_cast<size_t>(TN) * kBlockN * sizeof(int32_t));
   if (L.workspace == nullptr || L.workspace_bytes < need) return CB_ERR_WORKSPACE;
   // Ring depth: as many stages as ~200 KiB of shared memory holds.
