@@ -233,10 +233,10 @@ size_t cb_workspace_bytes(int op, int64_t batch, int64_t M, int64_t N, int64_t K
     case CB_OP_W4A16:
       return w4a16_workspace_bytes(batch, M, N, K);
     case CB_OP_W4A4: {
-      // unpacked A [M, K] and B [N, K] int8, then the int8 GEMM scratch.
+      // the int8 GEMM scratch, then unpacked A [M, K] and B [N, K] (8-bit).
       const size_t a = align_up(static_cast<size_t>(M) * K, 256);
       const size_t b = align_up(static_cast<size_t>(N) * K, 256);
-      return a + b + w8a8_workspace_bytes(1, M, N, K);
+      return align_up(w8a8_workspace_bytes(1, M, N, K), 256) + a + b;
     }
     default:
       return 0;
@@ -409,9 +409,12 @@ int cb_w4a4_gemm(const uint8_t* a_packed, const uint8_t* b_packed, float* c, int
   const size_t need = cb_workspace_bytes(CB_OP_W4A4, 1, M, N, K);
   if (!workspace || workspace_bytes < need) return CB_ERR_WORKSPACE;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  uint8_t* a8 = static_cast<uint8_t*>(workspace);
+  // The GEMM's split-K scratch sits at the start of the workspace, where every
+  // op keeps its (always re-zeroed) arrival counters; the unpacked operands follow.
+  const size_t gemm_bytes = align_up(w8a8_workspace_bytes(1, M, N, K), 256);
+  void* gemm_ws = workspace;
+  uint8_t* a8 = static_cast<uint8_t*>(workspace) + gemm_bytes;
   uint8_t* b8 = a8 + align_up(static_cast<size_t>(M) * K, 256);
-  void* gemm_ws = b8 + align_up(static_cast<size_t>(N) * K, 256);
   unpack_rows_i4_kernel<<<grid_for(M * K / 2, 256), 256, 0, s>>>(a_packed, lda, a8, M, K, wrap);
   unpack_cols_i4_kernel<<<grid_for(N * K / 2, 256), 256, 0, s>>>(b_packed, ldb, b8, K, N, wrap);
   if (cudaGetLastError() != cudaSuccess) return CB_ERR_CUDA;
@@ -433,7 +436,7 @@ int cb_w4a4_gemm(const uint8_t* a_packed, const uint8_t* b_packed, float* c, int
   L.out_sm = ldc;
   L.raw_f32 = 1;
   L.workspace = gemm_ws;
-  L.workspace_bytes = workspace_bytes - (static_cast<char*>(gemm_ws) - static_cast<char*>(workspace));
+  L.workspace_bytes = gemm_bytes;
   return launch_w8a8(L, s);
 }
 
