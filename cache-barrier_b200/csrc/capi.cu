@@ -186,6 +186,23 @@ int grid_for(long long total, int threads) {
 bool valid_out_dtype(int d) { return d == CB_DTYPE_F16 || d == CB_DTYPE_BF16 || d == CB_DTYPE_F32; }
 
 }  // namespace
+
+int validate_w8a8(const int8_t* aq, const int8_t* w, void* out, int out_dtype, int64_t batch, int64_t M,
+                  int64_t N, int64_t K, const int64_t* st) {
+  if (batch < 0 || M < 0 || N < 0 || K < 0) return CB_ERR_INVALID_ARG;
+  if (!st) return CB_ERR_INVALID_ARG;
+  if (batch * M * N == 0) return CB_OK;
+  if (!aq || !w || !out) return CB_ERR_INVALID_ARG;
+  if (!valid_out_dtype(out_dtype)) return CB_ERR_DTYPE;
+  if (K == 0 || K % 16 != 0) return CB_ERR_SHAPE;
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL || batch > 0xffffLL) return CB_ERR_TOO_LARGE;
+  if (!aligned16(aq) || !aligned16(w)) return CB_ERR_ALIGNMENT;
+  if (st[1] % 16 != 0 || st[3] % 16 != 0 || (batch > 1 && (st[0] % 16 != 0 || st[2] % 16 != 0)))
+    return CB_ERR_ALIGNMENT;
+  if (st[1] < K || st[3] < K) return CB_ERR_STRIDE;
+  return CB_OK;
+}
+
 }  // namespace cb
 
 using namespace cb;
@@ -267,22 +284,6 @@ int cb_quant_act_i8(const void* a, int a_dtype, int64_t batch, int64_t M, int64_
   if (K > 0x7fffffffLL || M > 0x7fffffffLL) return CB_ERR_TOO_LARGE;
   return launch_act_quant(a, a_dtype, batch, M, K, a_stride_b, a_stride_m, q, q_stride_b, q_stride_m, scale,
                           scale_stride_b, reinterpret_cast<cudaStream_t>(stream));
-}
-
-static int validate_w8a8(const int8_t* aq, const int8_t* w, void* out, int out_dtype, int64_t batch, int64_t M,
-                         int64_t N, int64_t K, const int64_t* st) {
-  if (batch < 0 || M < 0 || N < 0 || K < 0) return CB_ERR_INVALID_ARG;
-  if (!st) return CB_ERR_INVALID_ARG;
-  if (batch * M * N == 0) return CB_OK;
-  if (!aq || !w || !out) return CB_ERR_INVALID_ARG;
-  if (!valid_out_dtype(out_dtype)) return CB_ERR_DTYPE;
-  if (K == 0 || K % 16 != 0) return CB_ERR_SHAPE;
-  if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL || batch > 0xffffLL) return CB_ERR_TOO_LARGE;
-  if (!aligned16(aq) || !aligned16(w)) return CB_ERR_ALIGNMENT;
-  if (st[1] % 16 != 0 || st[3] % 16 != 0 || (batch > 1 && (st[0] % 16 != 0 || st[2] % 16 != 0)))
-    return CB_ERR_ALIGNMENT;
-  if (st[1] < K || st[3] < K) return CB_ERR_STRIDE;
-  return CB_OK;
 }
 
 int cb_w8a8_gemm(const int8_t* aq, const float* a_scale, const int8_t* w, const float* w_scale, void* out,

@@ -64,6 +64,10 @@ inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? CB_OK : CB_ERR
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Argument checks shared by the W8A8 entry points (strides as in cb_w8a8_gemm).
+int validate_w8a8(const int8_t* aq, const int8_t* w, void* out, int out_dtype, int64_t batch, int64_t M, int64_t N,
+                  int64_t K, const int64_t* st);
+
 // ---- launchers (validated arguments) ----
 int launch_act_quant(const void* a, int a_dtype, int64_t batch, int64_t M, int64_t K, int64_t a_sb, int64_t a_sm,
                      int8_t* q, int64_t q_sb, int64_t q_sm, float* scale, int64_t s_sb, cudaStream_t stream);

@@ -136,6 +136,20 @@ CB_API int cb_w8a8_gemm_dynamic(const void* a, int a_dtype, int8_t* q_buf, float
                          int64_t K, const int64_t* strides, void* workspace, size_t workspace_bytes,
                          cb_stream_t stream);
 
+/* Allocation-free variant of cb_w8a8_gemm (no counterpart in the reference).
+   For callers that cannot allocate device memory (another component owns all of
+   it, or a foreign-language binding has no allocator to call): same arguments and
+   results as cb_w8a8_gemm, without the workspace. The split-K scratch is an 8 MiB
+   device array inside this library, present on every GPU that loads it until the
+   process exits; problems needing more scratch than that (on a 148-SM B200: more
+   than 32 tokens) return CB_ERR_TOO_LARGE. The first call on a device looks the
+   array up with that device current; make it before any stream capture. All
+   calls on a device share the array: each clears its counters on its stream
+   first, and calls whose kernels overlap on the GPU race. */
+CB_API int cb_w8a8_gemm_noalloc(const int8_t* aq, const float* a_scale, const int8_t* w, const float* w_scale,
+                                void* out, int out_dtype, int32_t* acc_out, int64_t batch, int64_t M, int64_t N,
+                                int64_t K, const int64_t* strides, cb_stream_t stream);
+
 /* ---- W4A16 int4 group-dequant GEMM / batched INT4 BMM -------------------- */
 /* out[b, m, n] = sum_k a[b, m, k] * (q[b, k, n] * s[b, k / group_size, n]).
    Replaces kernel_batched_w4a16_simple / batched_int4_gemm
