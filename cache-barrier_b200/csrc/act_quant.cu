@@ -56,7 +56,10 @@ __global__ void __launch_bounds__(kThreads) act_quant_kernel(const T* __restrict
                                                               long long q_sb, long long q_sm,
                                                               float* __restrict__ scale, long long s_sb, int M,
                                                               int K, int vec_ok) {
+  // Release the dependent GEMM at once (it prefetches weights only), then wait
+  // for the preceding kernel before reading a or overwriting q and scale.
   pdl_launch_dependents();
+  pdl_wait_primary();
   __shared__ float red[kThreads / 32];
   const int row = blockIdx.x;
   const int b = row / M, m = row % M;
@@ -108,19 +111,30 @@ int launch_act_quant(const void* a, int a_dtype, int64_t batch, int64_t M, int64
   const size_t esz = 2;
   const int vec_ok = (K % 8 == 0) && aligned16(a) && ((a_sb * esz) % 16 == 0) && ((a_sm * esz) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(q) % 8 == 0) && (q_sb % 8 == 0) && (q_sm % 8 == 0);
-  dim3 grid(static_cast<unsigned>(rows));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(rows));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int Mi = static_cast<int>(M), Ki = static_cast<int>(K);
+  cudaError_t e;
   if (a_dtype == CB_DTYPE_BF16) {
-    act_quant_kernel<__nv_bfloat16><<<grid, kThreads, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(a), a_sb, a_sm, q, q_sb, q_sm, scale, s_sb, static_cast<int>(M),
-        static_cast<int>(K), vec_ok);
+    e = cudaLaunchKernelEx(&cfg, act_quant_kernel<__nv_bfloat16>, static_cast<const __nv_bfloat16*>(a),
+                           static_cast<long long>(a_sb), static_cast<long long>(a_sm), q, static_cast<long long>(q_sb),
+                           static_cast<long long>(q_sm), scale, static_cast<long long>(s_sb), Mi, Ki, vec_ok);
   } else if (a_dtype == CB_DTYPE_F16) {
-    act_quant_kernel<__half><<<grid, kThreads, 0, stream>>>(static_cast<const __half*>(a), a_sb, a_sm, q, q_sb,
-                                                             q_sm, scale, s_sb, static_cast<int>(M),
-                                                             static_cast<int>(K), vec_ok);
+    e = cudaLaunchKernelEx(&cfg, act_quant_kernel<__half>, static_cast<const __half*>(a), static_cast<long long>(a_sb),
+                           static_cast<long long>(a_sm), q, static_cast<long long>(q_sb), static_cast<long long>(q_sm),
+                           scale, static_cast<long long>(s_sb), Mi, Ki, vec_ok);
   } else {
     return CB_ERR_DTYPE;
   }
-  return cuda_status(cudaGetLastError());
+  return cuda_status(e);
 }
 
 }  // namespace cb

@@ -35,6 +35,44 @@ struct StreamK {
   }
 };
 
+// Coordinates of a k-block, advanced without division (the producer walks its
+// range one k-block at a time; 64-bit divisions per step would dominate it).
+struct KCursor {
+  int kb, h, nt, mt;
+  template <class P>
+  __device__ __forceinline__ void seek(const P& p, long long g) {
+    if (g < 0x7fffffffLL) {  // 32-bit divisions are several times cheaper
+      const unsigned gg = static_cast<unsigned>(g), kbt = static_cast<unsigned>(p.kb_per_tile);
+      const unsigned tile = gg / kbt, mtl = static_cast<unsigned>(p.m_tiles), ntl = static_cast<unsigned>(p.n_tiles);
+      kb = static_cast<int>(gg - tile * kbt);
+      mt = static_cast<int>(tile % mtl);
+      const unsigned r = tile / mtl;
+      nt = static_cast<int>(r % ntl);
+      h = static_cast<int>(r / ntl);
+      return;
+    }
+    const long long tile = g / p.kb_per_tile;
+    kb = static_cast<int>(g - tile * p.kb_per_tile);
+    mt = static_cast<int>(tile % p.m_tiles);
+    const long long r = tile / p.m_tiles;
+    nt = static_cast<int>(r % p.n_tiles);
+    h = static_cast<int>(r / p.n_tiles);
+  }
+  template <class P>
+  __device__ __forceinline__ void next(const P& p) {
+    if (++kb == p.kb_per_tile) {
+      kb = 0;
+      if (++mt == p.m_tiles) {
+        mt = 0;
+        if (++nt == p.n_tiles) {
+          nt = 0;
+          ++h;
+        }
+      }
+    }
+  }
+};
+
 // Output element store for the runtime-selected dtype.
 __device__ __forceinline__ void store_elem(void* out, int dtype, long long idx, float v) {
   if (dtype == CB_DTYPE_BF16) {

@@ -82,6 +82,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Acquire load of a counter in global memory (pairs with a writer's fence +
+// atomic increment).
+__device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+// Bounded wait until *ctr >= target (another CTA of the same grid publishes it).
+__device__ __forceinline__ bool wait_counter(const int* ctr, int target, volatile int* abort_flag, int* status) {
+  if (ld_acquire_gpu(ctr) >= target) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_gpu(ctr) >= target) return true;
+    if (abort_flag && *abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (abort_flag) *abort_flag = 1;
+      if (status) atomicOr(status, CB_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), single-CTA destination, completion on an mbarrier.
 // ----------------------------------------------------------------------------

@@ -55,6 +55,7 @@ struct Params {
   int scale_dtype;
   long long s_sb, s_sg;
   int group_size;
+  int kb_per_group;  // k-blocks of 128 per scale group (group_size / 128)
   int scale_in_epilogue;
   void* out;
   int out_dtype;
@@ -124,6 +125,27 @@ __device__ __forceinline__ void emit_row(const Params& p, int h, int n, int m0, 
   }
 }
 
+// Adds (in contributor order) the published parts of contributors [c_lo, c_hi]
+// (each its first segment, slot kind 0) for chunk c of this thread's row.
+template <int TN>
+__device__ __forceinline__ void sum_published(const Params& p, int c_lo, int c_hi, int c, int row, float (&v)[16]) {
+  for (int cc = c_lo; cc <= c_hi; cc += 4) {
+    float part[4][16];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c2 = cc + u;
+      const float* src = p.partials + static_cast<long long>(c2 * 2) * TN * kBlockN + (c * 16) * kBlockN + row;
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) part[u][jj] = c2 <= c_hi ? __ldcg(src + jj * kBlockN) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj)
+        if (cc + u <= c_hi) v[jj] = __fadd_rn(v[jj], part[u][jj]);
+  }
+}
+
 template <typename T, int TN>
 __global__ void __launch_bounds__(kThreads, 1)
     w4a16_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const Params p) {
@@ -154,6 +176,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long g1 = p.sk.start(blockIdx.x + 1);
 
   if (threadIdx.x == 0) {
+    // The next kernel in the stream may launch now: it only prefetches weights
+    // before its griddepcontrol.wait, which waits for this grid to complete.
+    pdl_launch_dependents();
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 5);  // 4 dequant warps + 1 MMA commit
@@ -172,6 +197,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     prefetch_tmap(&tmap_a);
   }
+  // Lanes of a warp reach every CTA-wide barrier together (aligned barriers
+  // count a warp as arrived when any of its lanes arrives).
+  __syncwarp();
   if (warp == 1) {
     __syncwarp();
     tmem_alloc(&tmem_base_sh, kTmemCols);
@@ -190,42 +218,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_a = policy_evict_last();
       const long long nmine = g1 - g0;
       const int pro = static_cast<int>(nmine < S ? nmine : S);
+      KCursor start_cur;
+      start_cur.seek(p, g0);
+      KCursor cur = start_cur;
+      auto wsrc = [&](const KCursor& c) {
+        return p.w + ((static_cast<long long>(c.h) * p.n_tiles + c.nt) * KB + c.kb) * kWTileBytes;
+      };
       for (int j = 0; j < pro; ++j) {
-        const long long g = g0 + j;
-        const long long tile = g / KB;
-        const int kb = static_cast<int>(g % KB);
-        int h, nt, mt;
-        decode_tile(p, tile, h, nt, mt);
-        const uint8_t* src = p.w + ((static_cast<long long>(h) * p.n_tiles + nt) * KB + kb) * kWTileBytes;
         mbar_arrive_expect_tx(&full_bar[j], kStageBytes);
-        bulk_copy_g2s(smem_w + j * kWTileBytes, src, kWTileBytes, &full_bar[j], pol_w);
+        bulk_copy_g2s(smem_w + j * kWTileBytes, wsrc(cur), kWTileBytes, &full_bar[j], pol_w);
+        cur.next(p);
       }
       pdl_wait_primary();
+      cur = start_cur;
       for (int j = 0; j < pro; ++j) {
-        const long long g = g0 + j;
-        const long long tile = g / KB;
-        const int kb = static_cast<int>(g % KB);
-        int h, nt, mt;
-        decode_tile(p, tile, h, nt, mt);
         uint8_t* dst = smem_a + j * kATileBytes;
-        tma_load_3d(dst, &tmap_a, &full_bar[j], kb * kBlockK, mt * TN, h, pol_a);
-        tma_load_3d(dst + kBoxBytes, &tmap_a, &full_bar[j], kb * kBlockK + 64, mt * TN, h, pol_a);
+        tma_load_3d(dst, &tmap_a, &full_bar[j], cur.kb * kBlockK, cur.mt * TN, cur.h, pol_a);
+        tma_load_3d(dst + kBoxBytes, &tmap_a, &full_bar[j], cur.kb * kBlockK + 64, cur.mt * TN, cur.h, pol_a);
+        cur.next(p);
       }
       int issued = pro;
       int stage = pro % S;
       uint32_t phase = (pro == S) ? 1u : 0u;
       for (long long g = g0 + pro; g < g1; ++g) {
         if (*abort_ptr || !mbar_wait(&empty_bar[stage], phase ^ 1u, abort_ptr, p.status)) break;
-        const long long tile = g / KB;
-        const int kb = static_cast<int>(g % KB);
-        int h, nt, mt;
-        decode_tile(p, tile, h, nt, mt);
-        const uint8_t* src = p.w + ((static_cast<long long>(h) * p.n_tiles + nt) * KB + kb) * kWTileBytes;
         mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
-        bulk_copy_g2s(smem_w + stage * kWTileBytes, src, kWTileBytes, &full_bar[stage], pol_w);
+        bulk_copy_g2s(smem_w + stage * kWTileBytes, wsrc(cur), kWTileBytes, &full_bar[stage], pol_w);
         uint8_t* dst = smem_a + stage * kATileBytes;
-        tma_load_3d(dst, &tmap_a, &full_bar[stage], kb * kBlockK, mt * TN, h, pol_a);
-        tma_load_3d(dst + kBoxBytes, &tmap_a, &full_bar[stage], kb * kBlockK + 64, mt * TN, h, pol_a);
+        tma_load_3d(dst, &tmap_a, &full_bar[stage], cur.kb * kBlockK, cur.mt * TN, cur.h, pol_a);
+        tma_load_3d(dst + kBoxBytes, &tmap_a, &full_bar[stage], cur.kb * kBlockK + 64, cur.mt * TN, cur.h, pol_a);
+        cur.next(p);
         ++issued;
         if (++stage == S) {
           stage = 0;
@@ -234,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       sh_issued = issued;
     }
+    __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
@@ -243,9 +266,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int n_tfull = 0;
       bool ok = true;
       long long g = g0;
+      int kb_first = static_cast<int>(g0 % KB);
+      int s = 0;
+      uint32_t ph = 0;
       while (g < g1 && ok) {
-        const long long tile = g / KB;
-        const long long seg_end = (tile + 1) * KB < g1 ? (tile + 1) * KB : g1;
+        const long long seg_len = (KB - kb_first) < (g1 - g) ? (KB - kb_first) : (g1 - g);
+        const long long seg_end = g + seg_len;
+        kb_first = 0;
         if (!mbar_wait(&tempty_bar, acc_phase ^ 1u, abort_ptr, p.status)) {
           ok = false;
           break;
@@ -254,8 +281,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool first = true;
         for (; g < seg_end; ++g) {
           const int j = static_cast<int>(g - g0);
-          const int s = j % S;
-          const uint32_t ph = static_cast<uint32_t>((j / S) & 1);
           const int b = j & (kNumABuf - 1);
           const uint32_t aph = static_cast<uint32_t>((j >> 2) & 1);
           if (*abort_ptr || !mbar_wait(&full_bar[s], ph, abort_ptr, p.status) ||
@@ -275,6 +300,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(&aempty_bar[b]);
           mma_commit(&empty_bar[s]);
           ++consumed;
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
         if (!ok) break;
         mma_commit(&tfull_bar);
@@ -294,6 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&aempty_bar[j & (kNumABuf - 1)], static_cast<uint32_t>((j >> 2) & 1), nullptr, p.status);
       if (n_tfull > 0) mbar_wait(&tfull_bar, static_cast<uint32_t>((n_tfull - 1) & 1), nullptr, p.status);
     }
+    __syncwarp();
   } else {
     // ---------------- dequant warpgroups (warps 2-5: group 0, 6-9: group 1) ----------------
     // Control flow stays uniform after an aborted wait (work is skipped, every
@@ -308,20 +338,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait_primary();
     uint32_t acc_phase = 0;
     long long g = g0;
-    while (g < g1) {
-      const long long tile = g / KB;
-      const int kb0 = static_cast<int>(g - tile * KB);
-      const long long seg_end = (tile + 1) * KB < g1 ? (tile + 1) * KB : g1;
-      const int kb1 = static_cast<int>(seg_end - tile * KB);
+    long long tile = g0 / KB;
+    int kb0 = static_cast<int>(g0 - tile * KB);
+    int s_next = 0;  // ring stage and phase of k-block j, advanced per k-block
+    uint32_t ph_next = 0;
+    for (; g < g1; ++tile, kb0 = 0) {
+      const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
+      const int kb1 = kb0 + static_cast<int>(seg_len);
       const bool first_seg = (g == g0);
       int h, nt, mt;
       decode_tile(p, tile, h, nt, mt);
       const int n = nt * kBlockN + row;
-      for (long long gg = g; gg < seg_end; ++gg) {
-        const int j = static_cast<int>(gg - g0);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int j = static_cast<int>(g - g0) + (kb - kb0);
+        const int s = s_next;
+        const uint32_t ph = ph_next;
+        if (++s_next == S) {
+          s_next = 0;
+          ph_next ^= 1u;
+        }
         if ((j & 1) != grp) continue;
-        const int s = j % S;
-        const uint32_t ph = static_cast<uint32_t>((j / S) & 1);
         const int b = j & (kNumABuf - 1);
         const uint32_t aph = static_cast<uint32_t>((j >> 2) & 1);
         bool got = mbar_wait(&full_bar[s], ph, abort_ptr, p.status);
@@ -331,8 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           typename Dq<T>::T2 sc = Dq<T>::from_f(1.0f);
           if (fold_scale) {
-            const int kb = static_cast<int>(gg - tile * KB);
-            const long long gi = static_cast<long long>(kb) * kBlockK / p.group_size;
+            const int gi = kb / p.kb_per_group;
             const float sv = n < p.N ? load_elem(p.scales, p.scale_dtype, h * p.s_sb + gi * p.s_sg + n) : 0.0f;
             sc = Dq<T>::from_f(sv);
           }
@@ -361,17 +396,47 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&empty_bar[s]);
         }
       }
-      g = seg_end;
+      g += seg_len;
       if (grp != 0) continue;
 
       // ---------------- epilogue (group 0) ----------------
+      const bool whole = (kb0 == 0 && kb1 == KB);
+      const int c_first = whole ? 0 : p.sk.owner(tile * KB);
+      const int c_last = whole ? 0 : p.sk.owner((tile + 1) * KB - 1);
+      const bool collect = !whole && static_cast<int>(blockIdx.x) == c_first;
+      constexpr bool kPrefetch = TN <= 32;
+      float other[kPrefetch ? TN : 1];
+      bool others_ready = true;
+      if (collect) {
+        // The other contributors handled this tile at the start of their ranges;
+        // wait (bounded) for all of them and pull their parts in before this
+        // CTA's own last MMAs complete.
+        if (threadIdx.x == 64) sh_is_last = wait_counter(&p.counters[c_first], c_last - c_first, abort_ptr, p.status);
+        named_bar_sync(1, 128);
+        others_ready = sh_is_last != 0;
+        if constexpr (kPrefetch) {
+#pragma unroll
+          for (int j = 0; j < TN; ++j) other[j] = 0.0f;
+          if (others_ready) {
+#pragma unroll
+            for (int c = 0; c < TN / 16; ++c) {
+              float v[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+              sum_published<TN>(p, c_first + 1, c_last, c, row, v);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) other[c * 16 + j] = v[j];
+            }
+          }
+        }
+      }
       const bool got = mbar_wait(&tfull_bar, acc_phase, abort_ptr, p.status);
       acc_phase ^= 1u;
       const bool live = __all_sync(0xffffffffu, got);
       tc_fence_after();
       const int m0 = mt * TN;
       const uint32_t d_addr = tmem_d + lane_off;
-      if (kb0 == 0 && kb1 == KB) {
+      if (whole) {
         if (live) {
 #pragma unroll 1
           for (int c = 0; c < TN / 16; ++c) {
@@ -388,7 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar);
-      } else {
+      } else if (!collect) {
+        // Partial tile, not its first contributor: publish this CTA's part.
         const int slot = blockIdx.x * 2 + (first_seg ? 0 : 1);
         float* dst = p.partials + static_cast<long long>(slot) * TN * kBlockN;
         if (live) {
@@ -407,42 +473,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&tempty_bar);
         __threadfence();
         named_bar_sync(1, 128);
-        const int c_first = p.sk.owner(tile * KB);
-        const int c_last = p.sk.owner((tile + 1) * KB - 1);
-        if (threadIdx.x == 64) {
-          int last = 0;
-          if (!*abort_ptr) {  // an aborted CTA never publishes an incomplete slot
-            const int prev = atomicAdd(&p.counters[c_first], 1);
-            last = (prev == c_last - c_first) ? 1 : 0;
-          }
-          sh_is_last = last;
-        }
-        named_bar_sync(1, 128);
-        if (sh_is_last) {
-          __threadfence();
-#pragma unroll 1
-          for (int c = 0; c < TN / 16; ++c) {
-            float v[16];
+        if (threadIdx.x == 64 && !*abort_ptr) atomicAdd(&p.counters[c_first], 1);
+      } else {
+        // Partial tile, first contributor: own accumulator + the others' parts.
+        if (live && others_ready) {
+          if constexpr (kPrefetch) {
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) v[jj] = 0.0f;
-            for (int cc = c_first; cc <= c_last; ++cc) {
-              const int sl = cc * 2 + p.sk.kind(cc, tile);
-              const float* src = p.partials + static_cast<long long>(sl) * TN * kBlockN;
+            for (int c = 0; c < TN / 16; ++c) {
+              uint32_t r[16];
+              __syncwarp();
+              tmem_ld16(d_addr + c * 16, r);
+              tmem_ld_wait();
+              float v[16];
 #pragma unroll
-              for (int jj = 0; jj < 16; ++jj) v[jj] = __fadd_rn(v[jj], __ldcg(src + (c * 16 + jj) * kBlockN + row));
+              for (int jj = 0; jj < 16; ++jj) v[jj] = __fadd_rn(__uint_as_float(r[jj]), other[c * 16 + jj]);
+              emit_row(p, h, n, m0, c * 16, v);
             }
-            emit_row(p, h, n, m0, c * 16, v);
+          } else {
+#pragma unroll 1
+            for (int c = 0; c < TN / 16; ++c) {
+              uint32_t r[16];
+              __syncwarp();
+              tmem_ld16(d_addr + c * 16, r);
+              tmem_ld_wait();
+              float v[16];
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) v[jj] = __uint_as_float(r[jj]);
+              sum_published<TN>(p, c_first + 1, c_last, c, row, v);
+              emit_row(p, h, n, m0, c * 16, v);
+            }
           }
-          named_bar_sync(1, 128);
-          if (threadIdx.x == 64) p.counters[c_first] = 0;
+          if (threadIdx.x == 64) p.counters[c_first] = 0;  // next launch starts from zero
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar);
       }
     }
   }
 
   __syncthreads();
-  if (threadIdx.x == 0 && abort_flag) {
-    for (int j = sh_consumed; j < sh_issued; ++j) mbar_wait(&full_bar[j % S], (j / S) & 1, nullptr, p.status);
+  if (warp == 0) {
+    if (lane == 0 && abort_flag) {
+      // Loads issued but never consumed must land before the CTA exits.
+      for (int j = sh_consumed; j < sh_issued; ++j) mbar_wait(&full_bar[j % S], (j / S) & 1, nullptr, p.status);
+    }
+    __syncwarp();
   }
   __syncthreads();
   if (warp == 1) {
@@ -543,6 +619,7 @@ int launch_w4a16(const W4A16Launch& L, cudaStream_t stream) {
   p.s_sg = L.s_sg;
   p.group_size = static_cast<int>(L.group_size);
   p.scale_in_epilogue = L.group_size >= L.K ? 1 : 0;
+  p.kb_per_group = static_cast<int>(L.group_size / kBlockK) > 0 ? static_cast<int>(L.group_size / kBlockK) : 1;
   p.out = L.out;
   p.out_dtype = L.out_dtype;
   p.out_sb = L.out_sb;

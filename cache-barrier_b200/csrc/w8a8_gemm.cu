@@ -62,17 +62,47 @@ __device__ __forceinline__ void decode_tile(const Params& p, long long tile, int
 template <int TN>
 __device__ __forceinline__ void emit_row(const Params& p, int h, int n, int m0, int t0, const int32_t (&v)[16]) {
   if (n >= p.N) return;
-  const float ws = p.raw_f32 ? 1.0f : p.w_scale[h * p.ws_sb + n];
+  // All scale loads are issued before any store: a load placed after a store
+  // that may alias it would otherwise wait for the previous iteration.
+  const float ws = p.raw_f32 ? 1.0f : __ldg(p.w_scale + h * p.ws_sb + n);
+  float as[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int m = m0 + t0 + j;
+    as[j] = (!p.raw_f32 && m < p.M) ? __ldg(p.a_scale + h * p.as_sb + m) : 1.0f;
+  }
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int m = m0 + t0 + j;
     if (m < p.M) {
       const long long idx = h * p.out_sb + static_cast<long long>(m) * p.out_sm + n;
       float f = __int2float_rn(v[j]);
-      if (!p.raw_f32) f = __fmul_rn(__fmul_rn(f, p.a_scale[h * p.as_sb + m]), ws);
+      if (!p.raw_f32) f = __fmul_rn(__fmul_rn(f, as[j]), ws);
       store_elem(p.out, p.out_dtype, idx, f);
       if (p.acc_out) p.acc_out[idx] = v[j];
     }
+  }
+}
+
+// Adds the published parts of contributors [c_lo, c_hi] (each its first
+// segment, slot kind 0) for chunk c of this thread's row; loads of four
+// contributors are in flight together.
+template <int TN>
+__device__ __forceinline__ void sum_published(const Params& p, int c_lo, int c_hi, int c, int row,
+                                              int32_t (&v)[16]) {
+  for (int cc = c_lo; cc <= c_hi; cc += 4) {
+    int32_t part[4][16];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c2 = cc + u;
+      const int32_t* src = p.partials + static_cast<long long>(c2 * 2) * TN * kBlockN + (c * 16) * kBlockN + row;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) part[u][j] = c2 <= c_hi ? __ldcg(src + j * kBlockN) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] += part[u][j];
   }
 }
 
@@ -105,6 +135,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long g1 = p.sk.start(blockIdx.x + 1);
 
   if (threadIdx.x == 0) {
+    // The next kernel in the stream may launch now: it only prefetches weights
+    // before its griddepcontrol.wait, which waits for this grid to complete.
+    pdl_launch_dependents();
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
@@ -115,11 +148,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     abort_flag = 0;
     sh_issued = 0;
     sh_consumed = 0;
-    sh_is_last = 0;
+    sh_is_last = 0;  // collector: whether every other contributor has published
     fence_mbar_init();
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_a);
   }
+  // Lanes of a warp reach every CTA-wide barrier together (aligned barriers
+  // count a warp as arrived when any of its lanes arrives).
+  __syncwarp();
   if (warp == 1) {
     __syncwarp();
     tmem_alloc(&tmem_base_sh, kTmemCols);
@@ -137,37 +173,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_a = policy_evict_last();
       const long long nmine = g1 - g0;
       const int pro = static_cast<int>(nmine < S ? nmine : S);
+      KCursor start_cur;
+      start_cur.seek(p, g0);
+      KCursor cur = start_cur;
       for (int j = 0; j < pro; ++j) {
-        const long long g = g0 + j;
-        const long long tile = g / KB;
-        const int kb = static_cast<int>(g % KB);
-        int h, nt, mt;
-        decode_tile(p, tile, h, nt, mt);
         mbar_arrive_expect_tx(&full_bar[j], kStageBytes);
-        tma_load_3d(smem_w + j * kWTileBytes, &tmap_w, &full_bar[j], kb * kBlockK, nt * kBlockN, h, pol_w);
+        tma_load_3d(smem_w + j * kWTileBytes, &tmap_w, &full_bar[j], cur.kb * kBlockK, cur.nt * kBlockN, cur.h,
+                    pol_w);
+        cur.next(p);
       }
       // Activations and scales are produced by the preceding kernel.
       pdl_wait_primary();
+      cur = start_cur;
       for (int j = 0; j < pro; ++j) {
-        const long long g = g0 + j;
-        const long long tile = g / KB;
-        const int kb = static_cast<int>(g % KB);
-        int h, nt, mt;
-        decode_tile(p, tile, h, nt, mt);
-        tma_load_3d(smem_a + j * kATileBytes, &tmap_a, &full_bar[j], kb * kBlockK, mt * TN, h, pol_a);
+        tma_load_3d(smem_a + j * kATileBytes, &tmap_a, &full_bar[j], cur.kb * kBlockK, cur.mt * TN, cur.h, pol_a);
+        cur.next(p);
       }
       int issued = pro;
       int stage = pro % S;
       uint32_t phase = (pro == S) ? 1u : 0u;
       for (long long g = g0 + pro; g < g1; ++g) {
         if (*abort_ptr || !mbar_wait(&empty_bar[stage], phase ^ 1u, abort_ptr, p.status)) break;
-        const long long tile = g / KB;
-        const int kb = static_cast<int>(g % KB);
-        int h, nt, mt;
-        decode_tile(p, tile, h, nt, mt);
         mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
-        tma_load_3d(smem_w + stage * kWTileBytes, &tmap_w, &full_bar[stage], kb * kBlockK, nt * kBlockN, h, pol_w);
-        tma_load_3d(smem_a + stage * kATileBytes, &tmap_a, &full_bar[stage], kb * kBlockK, mt * TN, h, pol_a);
+        tma_load_3d(smem_w + stage * kWTileBytes, &tmap_w, &full_bar[stage], cur.kb * kBlockK, cur.nt * kBlockN,
+                    cur.h, pol_w);
+        tma_load_3d(smem_a + stage * kATileBytes, &tmap_a, &full_bar[stage], cur.kb * kBlockK, cur.mt * TN, cur.h,
+                    pol_a);
+        cur.next(p);
         ++issued;
         if (++stage == S) {
           stage = 0;
@@ -176,6 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       sh_issued = issued;
     }
+    __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
@@ -186,9 +219,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int n_tfull = 0;
       bool ok = true;
       long long g = g0;
+      int kb_first = static_cast<int>(g0 % KB);
       while (g < g1 && ok) {
-        const long long tile = g / KB;
-        const long long seg_end = (tile + 1) * KB < g1 ? (tile + 1) * KB : g1;
+        const long long seg_len = (KB - kb_first) < (g1 - g) ? (KB - kb_first) : (g1 - g);
+        const long long seg_end = g + seg_len;
+        kb_first = 0;
         if (!mbar_wait(&tempty_bar, acc_phase ^ 1u, abort_ptr, p.status)) {
           ok = false;
           break;
@@ -232,6 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
       if (n_tfull > 0) mbar_wait(&tfull_bar, static_cast<uint32_t>((n_tfull - 1) & 1), nullptr, p.status);
     }
+    __syncwarp();
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     // Control flow is uniform across the 128 epilogue threads even after an
@@ -243,13 +279,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
     uint32_t acc_phase = 0;
     long long g = g0;
-    while (g < g1) {
-      const long long tile = g / KB;
-      const int kb0 = static_cast<int>(g - tile * KB);
-      const long long seg_end = (tile + 1) * KB < g1 ? (tile + 1) * KB : g1;
-      const int kb1 = static_cast<int>(seg_end - tile * KB);
+    long long tile = g0 / KB;
+    int kb0 = static_cast<int>(g0 - tile * KB);
+    for (; g < g1; ++tile, kb0 = 0) {
+      const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
+      const int kb1 = kb0 + static_cast<int>(seg_len);
       const bool first_seg = (g == g0);
-      g = seg_end;
+      g += seg_len;
+      const bool whole = (kb0 == 0 && kb1 == KB);
+      const int c_first = whole ? 0 : p.sk.owner(tile * KB);
+      const int c_last = whole ? 0 : p.sk.owner((tile + 1) * KB - 1);
+      const bool collect = !whole && static_cast<int>(blockIdx.x) == c_first;
+      constexpr bool kPrefetch = TN <= 32;
+      int32_t other[kPrefetch ? TN : 1];
+      bool others_ready = true;
+      if (collect) {
+        // The other contributors handled this tile at the start of their ranges;
+        // wait (bounded) for all of them, then pull their parts in while this
+        // CTA's own last MMAs are still running.
+        if (threadIdx.x == 64) sh_is_last = wait_counter(&p.counters[c_first], c_last - c_first, abort_ptr, p.status);
+        named_bar_sync(1, 128);
+        others_ready = sh_is_last != 0;
+        if constexpr (kPrefetch) {
+#pragma unroll
+          for (int j = 0; j < TN; ++j) other[j] = 0;
+          if (others_ready) {
+#pragma unroll
+            for (int c = 0; c < TN / 16; ++c) {
+              int32_t v[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = 0;
+              sum_published<TN>(p, c_first + 1, c_last, c, row, v);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) other[c * 16 + j] = v[j];
+            }
+          }
+        }
+      }
       const bool got = mbar_wait(&tfull_bar, acc_phase, abort_ptr, p.status);
       acc_phase ^= 1u;
       const bool live = __all_sync(0xffffffffu, got);
@@ -258,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       decode_tile(p, tile, h, nt, mt);
       const int n = nt * kBlockN + row;
       const int m0 = mt * TN;
-      if (kb0 == 0 && kb1 == KB) {
+      if (whole) {
         // Whole tile in this CTA: epilogue straight from TMEM.
         if (live) {
 #pragma unroll 1
@@ -276,8 +342,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar);
-      } else {
-        // Partial tile: write this CTA's slot, then the last contributor reduces.
+      } else if (!collect) {
+        // Partial tile, not its first contributor: publish this CTA's part
+        // (this is the CTA's first segment, long before the collector needs it).
         const int slot = blockIdx.x * 2 + (first_seg ? 0 : 1);
         int32_t* dst = p.partials + static_cast<long long>(slot) * TN * kBlockN;
         if (live) {
@@ -296,43 +363,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&tempty_bar);
         __threadfence();
         named_bar_sync(1, 128);
-        const int c_first = p.sk.owner(tile * KB);
-        const int c_last = p.sk.owner((tile + 1) * KB - 1);
-        if (threadIdx.x == 64) {
-          int last = 0;
-          if (!*abort_ptr) {  // an aborted CTA never publishes an incomplete slot
-            const int prev = atomicAdd(&p.counters[c_first], 1);
-            last = (prev == c_last - c_first) ? 1 : 0;
-          }
-          sh_is_last = last;
-        }
-        named_bar_sync(1, 128);
-        if (sh_is_last) {
-          __threadfence();
-#pragma unroll 1
-          for (int c = 0; c < TN / 16; ++c) {
-            int32_t v[16];
+        if (threadIdx.x == 64 && !*abort_ptr) atomicAdd(&p.counters[c_first], 1);
+      } else {
+        // Partial tile, first contributor (its last segment): the collector adds
+        // its own accumulator to the others' published parts and stores the tile.
+        if (live && others_ready) {
+          if constexpr (kPrefetch) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = 0;
-            for (int cc = c_first; cc <= c_last; ++cc) {
-              const int sl = cc * 2 + p.sk.kind(cc, tile);
-              const int32_t* src = p.partials + static_cast<long long>(sl) * TN * kBlockN;
+            for (int c = 0; c < TN / 16; ++c) {
+              uint32_t r[16];
+              __syncwarp();
+              tmem_ld16(lane_addr + c * 16, r);
+              tmem_ld_wait();
+              int32_t v[16];
 #pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] += __ldcg(src + (c * 16 + j) * kBlockN + row);
+              for (int j = 0; j < 16; ++j) v[j] = static_cast<int32_t>(r[j]) + other[c * 16 + j];
+              emit_row<TN>(p, h, n, m0, c * 16, v);
             }
-            emit_row<TN>(p, h, n, m0, c * 16, v);
+          } else {
+#pragma unroll 1
+            for (int c = 0; c < TN / 16; ++c) {
+              uint32_t r[16];
+              __syncwarp();
+              tmem_ld16(lane_addr + c * 16, r);
+              tmem_ld_wait();
+              int32_t v[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = static_cast<int32_t>(r[j]);
+              sum_published<TN>(p, c_first + 1, c_last, c, row, v);
+              emit_row<TN>(p, h, n, m0, c * 16, v);
+            }
           }
-          named_bar_sync(1, 128);
-          if (threadIdx.x == 64) p.counters[c_first] = 0;
+          if (threadIdx.x == 64) p.counters[c_first] = 0;  // next launch starts from zero
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar);
       }
     }
   }
 
   __syncthreads();
-  if (threadIdx.x == 0 && abort_flag) {
-    // Loads issued but never consumed must land before the CTA exits.
-    for (int j = sh_consumed; j < sh_issued; ++j) mbar_wait(&full_bar[j % S], (j / S) & 1, nullptr, p.status);
+  if (warp == 0) {
+    if (lane == 0 && abort_flag) {
+      // Loads issued but never consumed must land before the CTA exits.
+      for (int j = sh_consumed; j < sh_issued; ++j) mbar_wait(&full_bar[j % S], (j / S) & 1, nullptr, p.status);
+    }
+    __syncwarp();
   }
   __syncthreads();
   if (warp == 1) {
