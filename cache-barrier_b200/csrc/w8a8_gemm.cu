@@ -10,13 +10,16 @@
 // decode batches of 1..32 tokens still fill 128-row MMAs. Work is split over
 // all SMs with the stream-K partition of cb_gemm_common.cuh.
 //
-// Warp roles (192 threads):
+// Warp roles (224 threads):
 //   warp 0     TMA producer (one lane): weight tile 128 x 128 B + token tile TN x 128 B
 //              per k-block, 128-byte swizzle. Weight loads of the first ring pass
 //              are issued before griddepcontrol.wait; token loads after it.
 //   warp 1     TMEM allocation + MMA issuer (one lane), 4 MMAs (K = 32) per k-block.
 //   warps 2-5  epilogue: tcgen05.ld of the accumulator, scaling, bf16/f16/f32
 //              stores, split-K slot writes and the deterministic reduction.
+//   warp 6     stage waiter: waits for each stage's TMA bytes and hands the
+//              k-block to warp 1 through a named barrier, so the MMA issuer
+//              never waits on shared memory.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -30,7 +33,9 @@ namespace {
 
 constexpr int kBlockN = 128;   // weight rows per tile (MMA M)
 constexpr int kBlockK = 128;   // int8 K per k-block (one 128-byte swizzle row)
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;
+constexpr int kWaiterWarp = 6;
+constexpr int kHandoffBar = 2;  // named barrier: MMA warp + stage waiter (barrier 1 is the epilogue's)
 constexpr uint32_t kWTileBytes = kBlockN * kBlockK;
 
 struct Params {
@@ -193,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = pro % S;
       uint32_t phase = (pro == S) ? 1u : 0u;
       for (long long g = g0 + pro; g < g1; ++g) {
-        if (*abort_ptr || !mbar_wait(&empty_bar[stage], phase ^ 1u, abort_ptr, p.status)) break;
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_ptr, p.status)) break;
         mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
         tma_load_3d(smem_w + stage * kWTileBytes, &tmap_w, &full_bar[stage], cur.kb * kBlockK, cur.nt * kBlockN,
                     cur.h, pol_w);
@@ -210,31 +215,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      const uint32_t idesc = kUnsigned ? idesc_u8_s32(kBlockN, TN) : idesc_i8_s32(kBlockN, TN);
-      int stage = 0;
-      uint32_t phase = 0, acc_phase = 0;
-      int consumed = 0;
-      int n_tfull = 0;
-      bool ok = true;
-      long long g = g0;
-      int kb_first = static_cast<int>(g0 % KB);
-      while (g < g1 && ok) {
-        const long long seg_len = (KB - kb_first) < (g1 - g) ? (KB - kb_first) : (g1 - g);
-        const long long seg_end = g + seg_len;
-        kb_first = 0;
-        if (!mbar_wait(&tempty_bar, acc_phase ^ 1u, abort_ptr, p.status)) {
-          ok = false;
+    // ---------------- MMA issuer ----------------
+    // Lane 0 issues. The tensor core's instruction queue is shallow, so any
+    // stall of the issuing thread idles the tensor core; a shared-memory access
+    // (an mbarrier wait, a flag read) stalls it behind the tensor core's own
+    // operand reads. The stage-full waits are therefore done by warp 6, which
+    // hands each k-block over through a named barrier (no shared memory); the
+    // barrier's OR also carries a failed wait of either side, so both warps
+    // leave their loops at the same k-block.
+    const uint32_t idesc = kUnsigned ? idesc_u8_s32(kBlockN, TN) : idesc_i8_s32(kBlockN, TN);
+    int stage = 0;
+    uint32_t acc_phase = 0;
+    int consumed = 0;
+    int n_tfull = 0;
+    bool bad = false;
+    long long g = g0;
+    int kb_first = static_cast<int>(g0 % KB);
+    while (g < g1) {
+      const long long seg_len = (KB - kb_first) < (g1 - g) ? (KB - kb_first) : (g1 - g);
+      const long long seg_end = g + seg_len;
+      kb_first = 0;
+      // The epilogue must have drained the accumulator of the previous segment.
+      if (lane == 0) bad = !mbar_wait(&tempty_bar, acc_phase ^ 1u, abort_ptr, p.status);
+      bad = __shfl_sync(0xffffffffu, bad, 0);
+      acc_phase ^= 1u;
+      bool stop = false;
+      for (bool first = true; g < seg_end; ++g, first = false) {
+        if (named_bar_or(kHandoffBar, 64, bad)) {
+          stop = true;
           break;
         }
-        tc_fence_after();
-        bool first = true;
-        for (; g < seg_end; ++g) {
-          if (*abort_ptr || !mbar_wait(&full_bar[stage], phase, abort_ptr, p.status)) {
-            ok = false;
-            break;
-          }
+        if (lane == 0) {
           tc_fence_after();
           const uint32_t wa = smem_u32(smem_w + stage * kWTileBytes);
           const uint32_t aa = smem_u32(smem_a + stage * kATileBytes);
@@ -243,19 +254,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_i8_ss(tmem_d, smem_desc_sw128(wa + kk * 32), smem_desc_sw128(aa + kk * 32), idesc,
                       (first && kk == 0) ? 0u : 1u);
           }
-          first = false;
           mma_commit(&empty_bar[stage]);
-          ++consumed;
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1u;
-          }
         }
-        if (!ok) break;
-        mma_commit(&tfull_bar);
-        acc_phase ^= 1u;
-        ++n_tfull;
+        __syncwarp();
+        ++consumed;
+        if (++stage == S) stage = 0;
       }
+      if (stop) break;
+      if (lane == 0) mma_commit(&tfull_bar);
+      __syncwarp();
+      ++n_tfull;
+    }
+    if (lane == 0) {
       sh_consumed = consumed;
       // All issued MMAs must finish before TMEM is released.
       mma_commit(&drain_bar);
@@ -266,6 +276,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = consumed > S ? consumed - S : 0; j < consumed; ++j)
         mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
       if (n_tfull > 0) mbar_wait(&tfull_bar, static_cast<uint32_t>((n_tfull - 1) & 1), nullptr, p.status);
+    }
+    __syncwarp();
+  } else if (warp == kWaiterWarp) {
+    // ---------------- stage waiter ----------------
+    // Waits for each stage's TMA bytes and hands the k-block to the MMA warp
+    // (one named-barrier round per k-block, the same count as the MMA warp's).
+    int stage = 0;
+    uint32_t phase = 0;
+    for (long long g = g0; g < g1; ++g) {
+      bool bad = false;
+      if (lane == 0) bad = !mbar_wait(&full_bar[stage], phase, abort_ptr, p.status);
+      bad = __shfl_sync(0xffffffffu, bad, 0);
+      if (named_bar_or(kHandoffBar, 64, bad)) break;
+      if (++stage == S) {
+        stage = 0;
+        phase ^= 1u;
+      }
     }
     __syncwarp();
   } else {
