@@ -13,14 +13,19 @@
 //   2. a dequant warpgroup (4 warps, one weight row per thread) reads its row's
 //      64 bytes from shared memory, turns nibbles into bf16/f16 pairs with one
 //      LOP3 (mask + exponent-bias OR + sign flip) and one packed subtract, applies
-//      the group scale, and writes the 128 values straight into TMEM with
-//      tcgen05.st — the dequantized operand never goes back through shared
-//      memory;
-//   3. warp 1 issues 8 tcgen05.mma kind::f16 (K = 16 each) with A read from TMEM
-//      and B (tokens) from shared memory, accumulating fp32 in TMEM.
-// Two dequant warpgroups alternate k-blocks over four TMEM A buffers; the first
-// group also runs the epilogue. Split-K and the deterministic reduction are the
-// stream-K scheme of cb_gemm_common.cuh.
+//      the group scale, and stores the row into its A buffer in shared memory in
+//      the 128-byte-swizzled K-major layout the MMA reads;
+//   3. the warpgroup hands the buffer to warp 1 through a named barrier, and
+//      warp 1 issues 8 tcgen05.mma kind::f16 (K = 16 each, both operands from
+//      shared memory), accumulating fp32 in TMEM.
+// Three dequant warpgroups take every third k-block, each with its own A
+// buffer; the first group also runs the epilogue. Split-K and the
+// deterministic reduction are the stream-K scheme of cb_gemm_common.cuh.
+//
+// Throughput limit: moving the dequantized operand (32 KiB of 16-bit values per
+// k-block) through the SM costs about as much whether it is written to TMEM
+// (tcgen05.st, A read from TMEM) or to shared memory (A read by the MMA from
+// shared memory); both measured about 1.2K cycles per k-block per SM at T = 16.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -36,12 +41,18 @@ namespace {
 
 constexpr int kBlockN = 128;
 constexpr int kBlockK = 128;
-constexpr int kThreads = 320;  // producer, MMA, 2 x 4 dequant warps
+constexpr int kDqGroups = 3;  // dequant warpgroups; group g takes the k-blocks j with j % 3 == g
+constexpr int kThreads = (2 + 4 * kDqGroups) * 32;  // producer, MMA, 3 x 4 dequant warps
 constexpr uint32_t kWTileBytes = kBlockN * kBlockK / 2;  // 8 KiB
-constexpr int kNumABuf = 4;
-constexpr uint32_t kACols = kBlockK / 2;  // 32-bit TMEM columns per A buffer (2 x 16-bit per column)
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kDCol = kNumABuf * kACols;  // accumulator starts after the A buffers
+constexpr int kNumABuf = kDqGroups;  // shared-memory A buffer b belongs to dequant group b
+// One dequantized A tile: 128 rows x 128 k of 16-bit values, stored as two
+// 128-byte-swizzled K-major sub-tiles of 128 rows x 64 k (16 KiB each).
+constexpr uint32_t kASubBytes = kBlockN * 128;
+constexpr uint32_t kABufBytes = 2 * kASubBytes;
+// Named barriers 2..(1 + kNumABuf) hand A buffer b from dequant warpgroup b (4 warps,
+// bar.arrive) to the MMA warp (bar.sync); barrier 1 is the epilogue's.
+constexpr int kAFullBar0 = 2;
+constexpr int kAFullCount = 5 * 32;
 // Largest token tile used: 128 (M > 128 is covered by several 128-token tiles).
 constexpr int kMaxTokenTile = 128;
 
@@ -129,17 +140,17 @@ __device__ __forceinline__ void emit_row(const Params& p, int h, int n, int m0, 
 // (each its first segment, slot kind 0) for chunk c of this thread's row.
 template <int TN>
 __device__ __forceinline__ void sum_published(const Params& p, int c_lo, int c_hi, int c, int row, float (&v)[16]) {
-  for (int cc = c_lo; cc <= c_hi; cc += 4) {
-    float part[4][16];
+  for (int cc = c_lo; cc <= c_hi; cc += 2) {
+    float part[2][16];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 2; ++u) {
       const int c2 = cc + u;
       const float* src = p.partials + static_cast<long long>(c2 * 2) * TN * kBlockN + (c * 16) * kBlockN + row;
 #pragma unroll
       for (int jj = 0; jj < 16; ++jj) part[u][jj] = c2 <= c_hi ? __ldcg(src + jj * kBlockN) : 0.0f;
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < 2; ++u)
 #pragma unroll
       for (int jj = 0; jj < 16; ++jj)
         if (cc + u <= c_hi) v[jj] = __fadd_rn(v[jj], part[u][jj]);
@@ -152,11 +163,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kATileBytes = TN * kBlockK * 2;  // two 128-byte-swizzled boxes of TN x 64
   constexpr uint32_t kBoxBytes = TN * 128;
   constexpr uint32_t kStageBytes = kWTileBytes + kATileBytes;
+  constexpr uint32_t kTmemCols = TN < 32 ? 32 : TN;
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
-  __shared__ __align__(8) uint64_t afull_bar[kNumABuf];
   __shared__ __align__(8) uint64_t aempty_bar[kNumABuf];
   __shared__ __align__(8) uint64_t tfull_bar, tempty_bar, drain_bar;
   __shared__ uint32_t tmem_base_sh;
@@ -165,8 +176,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_ptr = &abort_flag;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* smem_a = smem;                              // token tiles (1024-aligned)
-  uint8_t* smem_w = smem + p.stages * kATileBytes;     // weight tiles
+  uint8_t* smem_abuf = smem;                                  // dequantized A tiles (1024-aligned)
+  uint8_t* smem_a = smem + kNumABuf * kABufBytes;             // token tiles (1024-aligned)
+  uint8_t* smem_w = smem_a + p.stages * kATileBytes;          // packed weight tiles
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -183,10 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 5);  // 4 dequant warps + 1 MMA commit
     }
-    for (int b = 0; b < kNumABuf; ++b) {
-      mbar_init(&afull_bar[b], 4);
-      mbar_init(&aempty_bar[b], 1);
-    }
+    for (int b = 0; b < kNumABuf; ++b) mbar_init(&aempty_bar[b], 1);
     mbar_init(&tfull_bar, 1);
     mbar_init(&tempty_bar, 4);
     mbar_init(&drain_bar, 1);
@@ -209,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
-  const uint32_t tmem_d = tmem_base + kDCol;
+  const uint32_t tmem_d = tmem_base;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -241,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = pro % S;
       uint32_t phase = (pro == S) ? 1u : 0u;
       for (long long g = g0 + pro; g < g1; ++g) {
-        if (*abort_ptr || !mbar_wait(&empty_bar[stage], phase ^ 1u, abort_ptr, p.status)) break;
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_ptr, p.status)) break;
         mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
         bulk_copy_g2s(smem_w + stage * kWTileBytes, wsrc(cur), kWTileBytes, &full_bar[stage], pol_w);
         uint8_t* dst = smem_a + stage * kATileBytes;
@@ -258,58 +267,56 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      const uint32_t idesc = idesc_f16_f32(kBlockN, TN, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
-      uint32_t acc_phase = 0;
-      int consumed = 0;
-      int n_tfull = 0;
-      bool ok = true;
-      long long g = g0;
-      int kb_first = static_cast<int>(g0 % KB);
-      int s = 0;
-      uint32_t ph = 0;
-      while (g < g1 && ok) {
-        const long long seg_len = (KB - kb_first) < (g1 - g) ? (KB - kb_first) : (g1 - g);
-        const long long seg_end = g + seg_len;
-        kb_first = 0;
-        if (!mbar_wait(&tempty_bar, acc_phase ^ 1u, abort_ptr, p.status)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        bool first = true;
-        for (; g < seg_end; ++g) {
-          const int j = static_cast<int>(g - g0);
-          const int b = j & (kNumABuf - 1);
-          const uint32_t aph = static_cast<uint32_t>((j >> 2) & 1);
-          if (*abort_ptr || !mbar_wait(&full_bar[s], ph, abort_ptr, p.status) ||
-              !mbar_wait(&afull_bar[b], aph, abort_ptr, p.status)) {
-            ok = false;
-            break;
-          }
+    // ---------------- MMA issuer ----------------
+    // A dequant warpgroup hands each filled TMEM A buffer over through a named
+    // barrier (it waited for the stage's TMA bytes first, so the token tile is
+    // in place too). The issuing thread then touches no shared memory per
+    // k-block: an access there stalls it behind the tensor core's operand
+    // reads, and the tensor core idles while its issuer is stalled. Every
+    // k-block's barrier is reached even after a failed wait, so the dequant
+    // warps never wait on a barrier this warp abandoned.
+    const uint32_t idesc = idesc_f16_f32(kBlockN, TN, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
+    uint32_t acc_phase = 0;
+    int consumed = 0;
+    int n_tfull = 0;
+    bool bad = false;
+    long long g = g0;
+    int kb_first = static_cast<int>(g0 % KB);
+    int s = 0;
+    while (g < g1) {
+      const long long seg_len = (KB - kb_first) < (g1 - g) ? (KB - kb_first) : (g1 - g);
+      const long long seg_end = g + seg_len;
+      kb_first = 0;
+      if (lane == 0 && !bad) bad = !mbar_wait(&tempty_bar, acc_phase ^ 1u, abort_ptr, p.status);
+      acc_phase ^= 1u;
+      for (bool first = true; g < seg_end; ++g, first = false) {
+        const int j = static_cast<int>(g - g0);
+        const int b = j % kNumABuf;
+        named_bar_sync(kAFullBar0 + b, kAFullCount);
+        if (lane == 0 && !bad) {
           tc_fence_after();
-          const uint32_t a_base = smem_u32(smem_a + s * kATileBytes);
-          const uint32_t a_tmem = tmem_base + b * kACols;
+          const uint32_t b_base = smem_u32(smem_a + s * kATileBytes);
+          const uint32_t w_base = smem_u32(smem_abuf + b * kABufBytes);
 #pragma unroll
           for (int i = 0; i < kBlockK / 16; ++i) {
-            const uint32_t baddr = a_base + (i >> 2) * kBoxBytes + (i & 3) * 32;
-            mma_f16_ts(tmem_d, a_tmem + i * 8, smem_desc_sw128(baddr), idesc, (first && i == 0) ? 0u : 1u);
+            const uint32_t waddr = w_base + (i >> 2) * kASubBytes + (i & 3) * 32;
+            const uint32_t baddr = b_base + (i >> 2) * kBoxBytes + (i & 3) * 32;
+            mma_f16_ss(tmem_d, smem_desc_sw128(waddr), smem_desc_sw128(baddr), idesc, (first && i == 0) ? 0u : 1u);
           }
-          first = false;
           mma_commit(&aempty_bar[b]);
           mma_commit(&empty_bar[s]);
           ++consumed;
-          if (++s == S) {
-            s = 0;
-            ph ^= 1u;
-          }
         }
-        if (!ok) break;
+        __syncwarp();
+        if (++s == S) s = 0;
+      }
+      if (lane == 0 && !bad) {
         mma_commit(&tfull_bar);
-        acc_phase ^= 1u;
         ++n_tfull;
       }
+      __syncwarp();
+    }
+    if (lane == 0) {
       sh_consumed = consumed;
       mma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, nullptr, p.status);
@@ -320,19 +327,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = consumed > S ? consumed - S : 0; j < consumed; ++j)
         mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
       for (int j = consumed > kNumABuf ? consumed - kNumABuf : 0; j < consumed; ++j)
-        mbar_wait(&aempty_bar[j & (kNumABuf - 1)], static_cast<uint32_t>((j >> 2) & 1), nullptr, p.status);
+        mbar_wait(&aempty_bar[j % kNumABuf], static_cast<uint32_t>((j / kNumABuf) & 1), nullptr, p.status);
       if (n_tfull > 0) mbar_wait(&tfull_bar, static_cast<uint32_t>((n_tfull - 1) & 1), nullptr, p.status);
     }
     __syncwarp();
   } else {
-    // ---------------- dequant warpgroups (warps 2-5: group 0, 6-9: group 1) ----------------
+    // ---------------- dequant warpgroups (warps 2-5: group 0, ..., 14-17: group 3) ----------------
     // Control flow stays uniform after an aborted wait (work is skipped, every
     // barrier arrival and named barrier still happens), so no warp is left
     // waiting on a collective that another warp abandoned.
     const int grp = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;  // TMEM lanes of this warp
     const typename Dq<T>::T2 bias = Dq<T>::bias();
     const bool fold_scale = !p.scale_in_epilogue;
     pdl_wait_primary();
@@ -349,6 +356,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       int h, nt, mt;
       decode_tile(p, tile, h, nt, mt);
       const int n = nt * kBlockN + row;
+      // Group scales are prefetched one k-block of this group ahead (a group
+      // takes every fourth k-block), so their global-load latency is off the
+      // dequant's critical path.
+      auto group_scale = [&](int kbx) {
+        return n < p.N ? load_elem(p.scales, p.scale_dtype, h * p.s_sb + (kbx / p.kb_per_group) * p.s_sg + n) : 0.0f;
+      };
+      const int kb_mine = kb0 + (grp - static_cast<int>((g - g0) % kDqGroups) + kDqGroups) % kDqGroups;  // this group's first
+      float sv_next = (fold_scale && kb_mine < kb1) ? group_scale(kb_mine) : 0.0f;
       for (int kb = kb0; kb < kb1; ++kb) {
         const int j = static_cast<int>(g - g0) + (kb - kb0);
         const int s = s_next;
@@ -357,44 +372,65 @@ __global__ void __launch_bounds__(kThreads, 1)
           s_next = 0;
           ph_next ^= 1u;
         }
-        if ((j & 1) != grp) continue;
-        const int b = j & (kNumABuf - 1);
-        const uint32_t aph = static_cast<uint32_t>((j >> 2) & 1);
+        if (j % kDqGroups != grp) continue;
+        const float sv = sv_next;
+        if (fold_scale && kb + kDqGroups < kb1) sv_next = group_scale(kb + kDqGroups);
+        const int b = grp;
+        const uint32_t aph = static_cast<uint32_t>((j / kNumABuf) & 1);
+        // Load the row's 64 bytes and dequantize the first half before waiting
+        // for the MMA to release this group's A buffer; only the TMEM stores
+        // depend on that release.
         bool got = mbar_wait(&full_bar[s], ph, abort_ptr, p.status);
+        const bool have = __all_sync(0xffffffffu, got);
+        const typename Dq<T>::T2 sc = Dq<T>::from_f(fold_scale ? sv : 1.0f);
+        uint4 v[4];
+        uint32_t r[32];
+        if (have) {
+          const uint4* wrow = reinterpret_cast<const uint4*>(smem_w + s * kWTileBytes + row * 64);
+          const int swz = (row >> 1) & 3;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) v[c] = wrow[c ^ swz];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t words[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+              for (int pi = 0; pi < 4; ++pi) r[c * 16 + wi * 4 + pi] = dq_pair<T>(words[wi], 4 * pi, bias, sc, fold_scale);
+          }
+        }
         got = mbar_wait(&aempty_bar[b], aph ^ 1u, abort_ptr, p.status) && got;
         const bool live = __all_sync(0xffffffffu, got);
         if (live) {
-          tc_fence_after();
-          typename Dq<T>::T2 sc = Dq<T>::from_f(1.0f);
-          if (fold_scale) {
-            const int gi = kb / p.kb_per_group;
-            const float sv = n < p.N ? load_elem(p.scales, p.scale_dtype, h * p.s_sb + gi * p.s_sg + n) : 0.0f;
-            sc = Dq<T>::from_f(sv);
-          }
-          const uint4* wrow = reinterpret_cast<const uint4*>(smem_w + s * kWTileBytes + row * 64);
-          const int swz = (row >> 1) & 3;
-          const uint32_t a_addr = tmem_base + lane_off + b * kACols;
+          // Row `row` of the A tile: 16-byte chunk q (k = 8q..8q+7) goes to
+          // sub-tile q / 8, chunk position (q % 8) ^ (row % 8) of the row's 128 bytes.
+          uint8_t* arow = smem_abuf + b * kABufBytes + row * 128;
+          const int rx = row & 7;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 v = wrow[c ^ swz];
-            uint32_t r[16];
-            const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<uint4*>(arow + (((q & 7) ^ rx) << 4)) =
+                make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
 #pragma unroll
-            for (int wi = 0; wi < 4; ++wi) {
+          for (int c = 2; c < 4; ++c) {
+            const uint32_t words[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+            uint32_t r2[16];
 #pragma unroll
-              for (int pi = 0; pi < 4; ++pi) r[wi * 4 + pi] = dq_pair<T>(words[wi], 4 * pi, bias, sc, fold_scale);
+            for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+              for (int pi = 0; pi < 4; ++pi) r2[wi * 4 + pi] = dq_pair<T>(words[wi], 4 * pi, bias, sc, fold_scale);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              const int q = (c - 2) * 4 + q4;  // chunk within sub-tile 1
+              *reinterpret_cast<uint4*>(arow + kASubBytes + ((q ^ rx) << 4)) =
+                  make_uint4(r2[4 * q4], r2[4 * q4 + 1], r2[4 * q4 + 2], r2[4 * q4 + 3]);
             }
-            __syncwarp();
-            tmem_st16(a_addr + c * 16, r);
           }
-          tmem_st_wait();
-          tc_fence_before();
+          // Generic-proxy stores become visible to the tensor core's reads.
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         }
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&afull_bar[b]);
-          mbar_arrive(&empty_bar[s]);
-        }
+        if (lane == 0) mbar_arrive(&empty_bar[s]);
+        named_bar_arrive(kAFullBar0 + b, kAFullCount);
       }
       g += seg_len;
       if (grp != 0) continue;
@@ -536,7 +572,7 @@ int launch_typed(const W4A16Launch& L, cudaStream_t stream, int grid, int stages
   int st = encode_tmap_3d(&ta, dt, L.a, static_cast<uint64_t>(L.K), static_cast<uint64_t>(L.M),
                           static_cast<uint64_t>(L.batch), L.a_sm, L.a_sb, 64, TN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != CB_OK) return st;
-  const size_t smem = static_cast<size_t>(stages) * (kWTileBytes + TN * kBlockK * 2) + 1024;
+  const size_t smem = kNumABuf * kABufBytes + static_cast<size_t>(stages) * (kWTileBytes + TN * kBlockK * 2) + 1024;
   static thread_local int configured_dev = -1;
   static thread_local size_t configured_smem = 0;
   int dev = 0;
@@ -605,7 +641,7 @@ int launch_w4a16(const W4A16Launch& L, cudaStream_t stream) {
   const size_t need = workspace_need(grid, static_cast<size_t>(TN) * kBlockN * sizeof(float));
   if (L.workspace == nullptr || L.workspace_bytes < need) return CB_ERR_WORKSPACE;
   const size_t stage_bytes = kWTileBytes + static_cast<size_t>(TN) * kBlockK * 2;
-  int stages = static_cast<int>((200u * 1024u) / stage_bytes);
+  int stages = static_cast<int>((220u * 1024u - kNumABuf * kABufBytes) / stage_bytes);
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) stages = 2;
   p.stages = stages;
