@@ -105,6 +105,9 @@ struct W4A16Launch {
   size_t workspace_bytes;
 };
 int launch_w4a16(const W4A16Launch& L, cudaStream_t stream);
+// Weight-stationary variant for long token dimensions and K <= 512 (w4a16_resident.cu).
+bool w4a16_resident_eligible(const W4A16Launch& L);
+int launch_w4a16_resident(const W4A16Launch& L, cudaStream_t stream);
 size_t w4a16_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K);
 
 }  // namespace cb

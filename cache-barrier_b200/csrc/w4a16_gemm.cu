@@ -32,6 +32,7 @@
 
 #include <type_traits>
 
+#include "cb_dequant.cuh"
 #include "cb_gemm_common.cuh"
 #include "cb_internal.h"
 #include "cb_ptx.cuh"
@@ -75,45 +76,6 @@ struct Params {
   int* counters;
   int* status;
 };
-
-template <typename T>
-struct Dq;
-template <>
-struct Dq<__nv_bfloat16> {
-  using T2 = __nv_bfloat162;
-  // 0x4300 = 128.0; nibble (offset by 8) lands in the low mantissa bits.
-  static constexpr uint32_t kOrXor = 0x43084308u;
-  static __device__ __forceinline__ T2 bias() { return __floats2bfloat162_rn(136.0f, 136.0f); }
-  static __device__ __forceinline__ T2 from_f(float f) { return __float2bfloat162_rn(f); }
-};
-template <>
-struct Dq<__half> {
-  using T2 = __half2;
-  // 0x6400 = 1024.0 in f16; ulp 1 in [1024, 2048).
-  static constexpr uint32_t kOrXor = 0x64086408u;
-  static __device__ __forceinline__ T2 bias() { return __floats2half2_rn(1032.0f, 1032.0f); }
-  static __device__ __forceinline__ T2 from_f(float f) { return __float2half2_rn(f); }
-};
-
-template <typename T>
-__device__ __forceinline__ uint32_t dq_pair(uint32_t word, int shift, typename Dq<T>::T2 bias,
-                                            typename Dq<T>::T2 sc, bool apply_scale) {
-  using T2 = typename Dq<T>::T2;
-  uint32_t bits = ((word >> shift) & 0x000F000Fu) ^ Dq<T>::kOrXor;
-  T2 v = *reinterpret_cast<T2*>(&bits);
-  v = __hsub2(v, bias);
-  if (apply_scale) v = __hmul2(v, sc);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
-__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
-                                              uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
-      : "memory");
-}
 
 __device__ __forceinline__ void decode_tile(const Params& p, long long tile, int& h, int& nt, int& mt) {
   mt = static_cast<int>(tile % p.m_tiles);
@@ -623,6 +585,11 @@ size_t w4a16_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K) {
 }
 
 int launch_w4a16(const W4A16Launch& L, cudaStream_t stream) {
+  if (L.batch == 0 || L.M == 0 || L.N == 0) return CB_OK;
+  if (w4a16_resident_eligible(L)) {
+    const int st = launch_w4a16_resident(L, stream);
+    if (st != CB_ERR_UNSUPPORTED) return st;
+  }
   const int TN = token_tile(L.M, kMaxTokenTile);
   Params p = {};
   p.M = static_cast<int>(L.M);

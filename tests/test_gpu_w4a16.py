@@ -142,3 +142,68 @@ def test_w4a16_repeat_is_deterministic(cuda_device):
     for _ in range(3):
         again = ops.w4a16_gemm(a_d, native, s_d, N, 128)
         assert torch.equal(first.view(torch.int16), again.view(torch.int16))
+
+
+# Shapes with M > 128 and K <= 512 take the weight-stationary kernel
+# (w4a16_resident.cu): the panel of 128 output columns is dequantized once per
+# CTA and the 128-row activation tiles stream past it.
+RESIDENT_SHAPES = [  # (B, M, N, K)
+    (1, 129, 128, 128),  # two m-tiles, the second with one row
+    (3, 6400, 384, 256),  # CTA ranges cross panel boundaries (a new panel is dequantized mid-range)
+    (16, 1000, 256, 512),  # MLA-like: two column panels per head, K = 512 (four resident k-blocks)
+    (2, 300, 200, 384),  # ragged N
+]
+
+
+@pytest.mark.parametrize("act_dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,M,N,K", RESIDENT_SHAPES)
+def test_w4a16_resident_g128(cuda_device, B, M, N, K, act_dtype):
+    """Same tolerance as the g128 decode path: max relative error <= 1e-2, rel-L2 <= 5e-3."""
+    from cb200 import _lib as L
+    from cb200 import ops
+    a, q, s = _int4_problem(B, M, N, K, 128, seed=B * 131 + M + N * 7 + K, act_dtype=act_dtype,
+                            scale_dtype=act_dtype)
+    ref = O.w4a16_gemm(to_np_f32(a), q.numpy(), to_np_f32(s), 128)
+    packed = torch.from_numpy(O.pack_u8_kn(q.numpy())).to(cuda_device)
+    native = ops.repack_w4(packed, L.CB_W4_REF_U8_KN, K, N)
+    out = ops.w4a16_gemm(a.to(cuda_device), native, s.to(cuda_device), N, 128)
+    torch.cuda.synchronize()
+    got = to_np_f32(out)
+    assert out.dtype == act_dtype and got.shape == (B, M, N)
+    assert max_rel(got, ref) <= 1e-2
+    assert rel_l2(got, ref) <= 5e-3
+    assert ops.device_status(cuda_device) == 0
+
+
+@pytest.mark.parametrize("B,M,N,K", [(2, 300, 200, 256), (4, 1024, 128, 512)])
+def test_w4a16_resident_per_channel_fp16_f32out(cuda_device, B, M, N, K):
+    """Per-channel scale applied to the fp32 accumulator in the epilogue; fp32 output.
+    max |got - ref| <= 2e-3 * max |ref| and rel-L2 <= 1e-3 (as the decode path)."""
+    from cb200 import _lib as L
+    from cb200 import ops
+    g = torch.Generator().manual_seed(M + N + K)
+    a = (torch.randn(B, M, K, generator=g) / 4).half()
+    q = torch.randint(-8, 8, (B, K, N), generator=g, dtype=torch.int32).to(torch.int8)
+    s = ((torch.randn(B, N, generator=g) * 0.05).abs() + 1e-3).half()
+    ref = O.w4a16_per_channel(a.float().numpy(), q.numpy(), s.float().numpy())
+    packed = torch.from_numpy(O.pack_u8_kn(q.numpy())).to(cuda_device)
+    native = ops.repack_w4(packed, L.CB_W4_REF_U8_KN, K, N)
+    out = ops.w4a16_gemm(a.to(cuda_device), native, s.to(cuda_device), N, group_size=K, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    assert out.dtype == torch.float32
+    assert max_rel(got, ref) <= 2e-3
+    assert rel_l2(got, ref) <= 1e-3
+    assert ops.device_status(cuda_device) == 0
+
+
+def test_w4a16_resident_deterministic(cuda_device):
+    from cb200 import _lib as L
+    from cb200 import ops
+    a, q, s = _int4_problem(16, 777, 256, 512, 128, seed=5)
+    native = ops.repack_w4(torch.from_numpy(O.pack_u8_kn(q.numpy())).to(cuda_device), L.CB_W4_REF_U8_KN, 512, 256)
+    a_d, s_d = a.to(cuda_device), s.to(cuda_device)
+    o1 = ops.w4a16_gemm(a_d, native, s_d, 256, 128)
+    o2 = ops.w4a16_gemm(a_d, native, s_d, 256, 128)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)
