@@ -70,6 +70,13 @@ SIGNATURES = {
     "cb_repack_w4": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _vp]),
     "cb_w4_native_bytes": (_sz, [_i64, _i64, _i64]),
     "cb_repack_w8_kmajor": (_int, [_vp, _vp, _i64, _i64, _i64, _vp]),
+    "cb_symm_bytes": (_sz, [_int, _i64]),
+    "cb_symm_alloc": (_int, [_sz, ctypes.POINTER(_vp)]),
+    "cb_symm_free": (_int, [_vp]),
+    "cb_ipc_get_handle": (_int, [_vp, _vp]),
+    "cb_ipc_open_handle": (_int, [_vp, ctypes.POINTER(_vp)]),
+    "cb_ipc_close_handle": (_int, [_vp]),
+    "cb_peer_allreduce": (_int, [_vp, _vp, _i64, _int, _vp, _int, _int, _i64, _vp, _vp]),
 }
 
 _lock = threading.Lock()

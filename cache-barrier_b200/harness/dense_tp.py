@@ -164,9 +164,10 @@ class TPStack:
     """The layers' weight shards of one rank, and one decode step over them."""
 
     def __init__(self, d: Dims, tp: int, rank: int, backend: Backend, device, seed: int = 0,
-                 full_weights=None, group=None):
+                 full_weights=None, group=None, allreduce=None):
         self.d, self.tp, self.rank, self.backend = d, tp, rank, backend
         self.device, self.group = device, group
+        self.allreduce = allreduce  # None: NCCL through torch.distributed; else a callable(x, out=x)
         self.handles = []
         for layer in range(d.layers):
             hs = {}
@@ -205,11 +206,17 @@ class TPStack:
         b.run(self.x, h["qkv"], self.qkv_out, sc)
         b.run(self.o_in, h["o"], self.o_out, sc)
         if reduce and self.tp > 1:
-            dist.all_reduce(self.o_out, group=self.group)
+            self._reduce(self.o_out)
         b.run(self.x, h["gate_up"], self.gu_out, sc)
         b.run(self.act_in, h["down"], self.d_out, sc)
         if reduce and self.tp > 1:
-            dist.all_reduce(self.d_out, group=self.group)
+            self._reduce(self.d_out)
+
+    def _reduce(self, t):
+        if self.allreduce is None:
+            dist.all_reduce(t, group=self.group)
+        else:
+            self.allreduce(t, out=t)
 
     def step(self, reduce: bool = True):
         for i in range(self.d.layers):
@@ -256,6 +263,7 @@ def main():
     ap.add_argument("--layers", type=int, default=64)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--allreduce", default="nccl", help="comma-separated: nccl, peer (NVLink one-shot kernel)")
     ap.add_argument("--out", default=None)
     args = ap.parse_args()
 
@@ -269,19 +277,28 @@ def main():
     from common import ClockSampler, gpu_info, save_json
 
     d = Dims(layers=args.layers)
+    tokens = [int(t) for t in args.tokens.split(",")]
+    modes = args.allreduce.split(",") if world > 1 else ["none"]
+    peer = None
+    if "peer" in modes:
+        sys.path.insert(0, os.path.dirname(HERE))
+        from cb200.peer import PeerAllReduce
+
+        peer = PeerAllReduce(max(tokens) * d.hidden, device=dev)
     rows = []
     for prec in args.precisions.split(","):
         backend = BACKENDS[prec]()
         stack = TPStack(d, world, rank, backend, dev, seed=1234)
-        for T in [int(t) for t in args.tokens.split(",")]:
+        for T, mode in [(T, m) for T in tokens for m in modes]:
             stack.bind(T)
+            stack.allreduce = peer if mode == "peer" else None
             if world > 1:
                 dist.barrier()
             with ClockSampler(local) as clk:
                 ms = _max_over_ranks(_time_graph(lambda: stack.step(True), args.steps, args.warmup), dev)
                 ms_noar = _max_over_ranks(_time_graph(lambda: stack.step(False), args.steps, args.warmup), dev)
             wb = stack.weight_bytes()
-            row = {"precision": prec, "tokens": T, "tp": world, "layers": d.layers,
+            row = {"precision": prec, "tokens": T, "tp": world, "layers": d.layers, "allreduce": mode,
                    "step_ms": round(ms, 4), "us_per_layer": round(ms * 1e3 / d.layers, 3),
                    "step_ms_without_allreduce": round(ms_noar, 4),
                    "allreduce_us_per_layer": round((ms - ms_noar) * 1e3 / d.layers, 3),
@@ -291,7 +308,7 @@ def main():
                    "clocks": clk.info}
             rows.append(row)
             if rank == 0:
-                print(f"tp={world} {prec:6s} T={T:3d}: {row['us_per_layer']:9.2f} us/layer "
+                print(f"tp={world} {prec:6s} T={T:3d} [{mode}]: {row['us_per_layer']:9.2f} us/layer "
                       f"(all-reduce {row['allreduce_us_per_layer']:.2f}), {row['weight_gbs_per_gpu']} GB/s/GPU",
                       flush=True)
         del stack
@@ -303,6 +320,9 @@ def main():
                "rows": rows}
         if args.out:
             save_json(args.out, out)
+    if peer is not None:
+        assert int(peer.status.item()) == 0, "peer all-reduce reported a timeout"
+        peer.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -198,6 +198,29 @@ CB_API size_t cb_w4_native_bytes(int64_t batch, int64_t K, int64_t N);
 CB_API int cb_repack_w8_kmajor(const int8_t* src_kn, int8_t* dst_nk, int64_t batch, int64_t K, int64_t N,
                         cb_stream_t stream);
 
+/* ---- One-shot all-reduce over NVLink peer memory (tensor-parallel projections) ----
+ * No counterpart in the reference, which has no multi-GPU code: it replaces the
+ * NCCL all-reduce after the row-parallel O and down projections of a
+ * tensor-parallel decoder for small [T, hidden] 16-bit partials.
+ *
+ * Setup (once per rank, all ranks alike): cb_symm_alloc(cb_symm_bytes(world,
+ * slot_elems)) gives this rank's zeroed symmetric area; cb_ipc_get_handle
+ * exports it as a 64-byte CUDA IPC handle, the host exchanges handles, and
+ * cb_ipc_open_handle maps every peer's area. cb_peer_allreduce(in, out, elems,
+ * dtype, areas[world], rank, world, slot_elems, status, stream) then sums the
+ * world partials `in` into `out` on every rank (same values on all ranks, fp32
+ * sums in rank order). Every rank must issue the same sequence of calls with the
+ * same element counts. A peer that never joins makes the call return after about
+ * a second with CB_DEVERR_TIMEOUT set in *status (a device int). */
+CB_API size_t cb_symm_bytes(int world, int64_t slot_elems);
+CB_API int cb_symm_alloc(size_t bytes, void** ptr);
+CB_API int cb_symm_free(void* ptr);
+CB_API int cb_ipc_get_handle(const void* dev_ptr, void* handle_out /* 64 bytes */);
+CB_API int cb_ipc_open_handle(const void* handle_in /* 64 bytes */, void** peer_ptr);
+CB_API int cb_ipc_close_handle(void* peer_ptr);
+CB_API int cb_peer_allreduce(const void* in, void* out, int64_t elems, int dtype, void* const* symm_areas, int rank,
+                             int world, int64_t slot_elems, int* status, cb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
