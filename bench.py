@@ -411,6 +411,13 @@ def main():
         cpu = {"value": round(mean_s * 1e6, 1), "unit": UNIT, "cores": cores, "kind": "port",
                "sample": "T=1,8,16,32 x 3 timed reps each (median), K=N=8192: per-token quant, exact int GEMM "
                          "(numpy fp64 BLAS), fp32 epilogue, bf16 cast"}
+        # the W4A16 CPU configuration: T=16, K=N=4096, int4 g128 bf16 scales, explicit dequant + matmul
+        p4 = CB.W4A16Cpu(4096, 4096, 128, seed=0)
+        m4, _ = CB.time_path(p4, [16], reps=5, warmup=1)
+        if isinstance(w4, dict) and "error" not in w4:
+            w4["cpu_baseline"] = {"value": round(m4 * 1e6, 1), "unit": UNIT, "cores": cores, "kind": "port",
+                                  "sample": "T=16, K=N=4096 int4 g128: explicit dequant (part of the timed path) "
+                                            "+ fp32 matmul + bf16 cast, median of 5"}
         del ctl
 
     assert ops.device_status(dev) == 0

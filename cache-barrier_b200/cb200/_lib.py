@@ -70,6 +70,8 @@ SIGNATURES = {
     "cb_repack_w4": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _vp]),
     "cb_w4_native_bytes": (_sz, [_i64, _i64, _i64]),
     "cb_repack_w8_kmajor": (_int, [_vp, _vp, _i64, _i64, _i64, _vp]),
+    "cb_rmsnorm_quant_i8": (_int, [_vp, _int, _vp, _int, ctypes.c_float, _i64, _i64, _i64, _vp, _i64, _vp, _vp,
+                                   _i64, _vp]),
     "cb_symm_bytes": (_sz, [_int, _i64]),
     "cb_symm_alloc": (_int, [_sz, ctypes.POINTER(_vp)]),
     "cb_symm_free": (_int, [_vp]),

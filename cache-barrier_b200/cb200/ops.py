@@ -135,6 +135,37 @@ def quant_act_i8(a: torch.Tensor, q: torch.Tensor | None = None, s: torch.Tensor
     return q, s
 
 
+def rmsnorm_quant_i8(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, q: torch.Tensor | None = None,
+                     s: torch.Tensor | None = None, y: torch.Tensor | None = None):
+    """Fused RMSNorm + per-token int8 quantization of ``x`` ([rows, H], f16/bf16).
+
+    Returns ``(q, s)`` (int8 like x, fp32 ``[rows]``) exactly as ``quant_act_i8``
+    applied to the RMSNorm output ``cvt(x * rsqrt(mean(x^2) + eps) * weight)``;
+    ``y`` (optional, like x) receives that output.
+    """
+    _require_cuda(x, weight, q, s, y)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be [rows, H], contiguous along H")
+    rows, H = x.shape
+    if weight.numel() != H or not weight.is_contiguous():
+        raise ValueError("weight must be a contiguous [H] tensor")
+    if q is None:
+        q = torch.empty(rows, H, dtype=torch.int8, device=x.device)
+    if s is None:
+        s = torch.empty(rows, dtype=torch.float32, device=x.device)
+    if q.shape != (rows, H) or q.dtype != torch.int8 or q.stride(1) != 1:
+        raise ValueError("q must be int8 [rows, H], contiguous along H")
+    if s.dtype != torch.float32 or s.numel() < rows or not s.is_contiguous():
+        raise ValueError("s must be a contiguous fp32 tensor of at least rows elements")
+    if y is not None and (y.shape != (rows, H) or y.dtype != x.dtype or y.stride(1) != 1):
+        raise ValueError("y must be like x")
+    code = L.load().cb_rmsnorm_quant_i8(x.data_ptr(), dtype_code(x.dtype), weight.data_ptr(), dtype_code(weight.dtype),
+                                        float(eps), rows, H, x.stride(0), q.data_ptr(), q.stride(0), s.data_ptr(),
+                                        _ptr(y), y.stride(0) if y is not None else 0, _stream(x.device))
+    L.check("cb_rmsnorm_quant_i8", code)
+    return q, s
+
+
 # ---------------------------------------------------------------------------
 # W8A8
 # ---------------------------------------------------------------------------

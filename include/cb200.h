@@ -198,6 +198,16 @@ CB_API size_t cb_w4_native_bytes(int64_t batch, int64_t K, int64_t N);
 CB_API int cb_repack_w8_kmajor(const int8_t* src_kn, int8_t* dst_nk, int64_t batch, int64_t K, int64_t N,
                         cb_stream_t stream);
 
+/* Fused RMSNorm -> dynamic per-token int8 quantization (no counterpart kernel in
+   the reference, which measures this fusion with library ops:
+   profiling/mechanisms/RESULTS.md:17). Per row of x [rows, H] (f16/bf16, row
+   stride x_sm): r = 1/sqrt(sum x^2 / H + eps) in fp32; y = cvt(x * r * w) in x's
+   dtype; then scale and q exactly as cb_quant_act_i8 on y. weight: [H] f16, bf16
+   or f32. y_out (nullable, row stride y_sm) receives y. */
+CB_API int cb_rmsnorm_quant_i8(const void* x, int x_dtype, const void* weight, int w_dtype, float eps, int64_t rows,
+                               int64_t H, int64_t x_sm, int8_t* q, int64_t q_sm, float* scale, void* y_out,
+                               int64_t y_sm, cb_stream_t stream);
+
 /* ---- One-shot all-reduce over NVLink peer memory (tensor-parallel projections) ----
  * No counterpart in the reference, which has no multi-GPU code: it replaces the
  * NCCL all-reduce after the row-parallel O and down projections of a

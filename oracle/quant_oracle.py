@@ -289,3 +289,22 @@ def unpack_native(buf: np.ndarray, B: int, K: int, N: int) -> np.ndarray:
     # [B, nt, kt, r, chunk, word, j] -> [B, kt*128, nt*128]
     vals = vals.reshape(B, nt, kt, 128, 128).transpose(0, 2, 4, 1, 3).reshape(B, kt * 128, nt * 128)
     return vals[:, :K, :N].astype(np.int8)
+
+
+def rmsnorm_quant_i8(x_bits_or_f32, weight_f32, eps, dtype="bf16"):
+    """Fused RMSNorm + per-token int8 quantization (csrc/rmsnorm_quant.cu):
+    r = 1/sqrt(sum x^2 / H + eps) in fp32, y = round_to_dtype(x * r * w), then the
+    act-quant rules of quant_act_i8 on y. x is given as float32 values of a
+    16-bit tensor [rows, H]. Returns (q int8, scale fp32, y float32 values).
+    No reference kernel exists for this fusion (the reference measures it with
+    library ops, profiling/mechanisms/RESULTS.md:17); the quantization step is
+    the pinned act-quant restatement."""
+    x = np.asarray(x_bits_or_f32, dtype=np.float32)
+    w = np.asarray(weight_f32, dtype=np.float32)
+    H = x.shape[-1]
+    ss = np.sum(x * x, axis=-1, dtype=np.float32)
+    r = (np.float32(1.0) / np.sqrt(ss / np.float32(H) + np.float32(eps))).astype(np.float32)
+    yf = ((x * r[..., None]).astype(np.float32) * w).astype(np.float32)
+    y = bf16_bits_to_f32(f32_to_bf16_bits(yf)) if dtype == "bf16" else yf.astype(np.float16).astype(np.float32)
+    q, s = quant_act_i8(y)
+    return q, s, y
