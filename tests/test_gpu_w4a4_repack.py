@@ -71,3 +71,26 @@ def test_quantize_weights_w8_gpu_view_layout(cuda_device, golden):
     expect = np.clip(np.rint(d["w"].astype(np.float32) / s_np[:, None, :]), -127, 127).astype(np.int8)
     assert np.array_equal(q.cpu().numpy(), expect)
     assert (q.cpu().numpy() == d["wq"]).mean() > 0.999
+
+
+def test_host_packer_matches_device_repack_and_runs(cuda_device, tmp_path):
+    """The offline packer (cb200.wformat) writes the bytes cb_repack_w4 produces;
+    weights loaded from a file run in the W4A16 GEMM with identical results."""
+    from cb200 import _lib as L
+    from cb200 import ops, wformat
+
+    rng = np.random.default_rng(3)
+    B, K, N, T = 2, 384, 200, 5
+    q = rng.integers(-8, 8, size=(B, K, N)).astype(np.int8)
+    packed = O.pack_u8_kn(q)
+    dev_native = ops.repack_w4(torch.from_numpy(packed).to(cuda_device), L.CB_W4_REF_U8_KN, K, N)
+    s = torch.from_numpy((np.abs(rng.standard_normal((B, K // 128, N))) * 0.01 + 1e-3).astype(np.float32)).to(torch.bfloat16)
+    p = wformat.pack_int4(packed, wformat.W4_REF_U8_KN, K, N, s, 128)
+    assert np.array_equal(p.native, dev_native.cpu().numpy())
+    wformat.save(str(tmp_path / "w.cbw"), {"w": p})
+    got = wformat.load(str(tmp_path / "w.cbw"), device=cuda_device)["w"]
+    a = torch.randn(B, T, K, device=cuda_device).to(torch.bfloat16)
+    o1 = ops.w4a16_gemm(a, dev_native, s.to(cuda_device), N, 128)
+    o2 = ops.w4a16_gemm(a, got.native, got.scales, N, 128)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)
