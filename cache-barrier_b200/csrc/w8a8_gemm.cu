@@ -161,6 +161,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Lanes of a warp reach every CTA-wide barrier together (aligned barriers
   // count a warp as arrived when any of its lanes arrives).
   __syncwarp();
+  // First ring pass of weight loads: lane j of warp 0 issues stage j, as soon as
+  // the barriers exist and before the CTA-wide setup (TMEM allocation), so the
+  // weight stream starts within a few hundred cycles of the CTA's launch.
+  const long long nmine = g1 - g0;
+  const int pro = static_cast<int>(nmine < S ? nmine : S);
+  const uint64_t pol_w = policy_evict_first();
+  if (warp == 0 && lane < pro) {
+    KCursor c;
+    c.seek(p, g0 + lane);
+    mbar_arrive_expect_tx(&full_bar[lane], kStageBytes);
+    tma_load_3d(smem_w + lane * kWTileBytes, &tmap_w, &full_bar[lane], c.kb * kBlockK, c.nt * kBlockN, c.h, pol_w);
+  }
+  __syncwarp();
   if (warp == 1) {
     __syncwarp();
     tmem_alloc(&tmem_base_sh, kTmemCols);
@@ -172,28 +185,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_d = tmem_base_sh;
 
   if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    const uint64_t pol_a = policy_evict_last();
+    // Activations and scales are produced by the preceding kernel.
+    pdl_wait_primary();
+    if (lane < pro) {
+      KCursor c;
+      c.seek(p, g0 + lane);
+      tma_load_3d(smem_a + lane * kATileBytes, &tmap_a, &full_bar[lane], c.kb * kBlockK, c.mt * TN, c.h, pol_a);
+    }
+    __syncwarp();
     if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      const uint64_t pol_w = policy_evict_first();
-      const uint64_t pol_a = policy_evict_last();
-      const long long nmine = g1 - g0;
-      const int pro = static_cast<int>(nmine < S ? nmine : S);
-      KCursor start_cur;
-      start_cur.seek(p, g0);
-      KCursor cur = start_cur;
-      for (int j = 0; j < pro; ++j) {
-        mbar_arrive_expect_tx(&full_bar[j], kStageBytes);
-        tma_load_3d(smem_w + j * kWTileBytes, &tmap_w, &full_bar[j], cur.kb * kBlockK, cur.nt * kBlockN, cur.h,
-                    pol_w);
-        cur.next(p);
-      }
-      // Activations and scales are produced by the preceding kernel.
-      pdl_wait_primary();
-      cur = start_cur;
-      for (int j = 0; j < pro; ++j) {
-        tma_load_3d(smem_a + j * kATileBytes, &tmap_a, &full_bar[j], cur.kb * kBlockK, cur.mt * TN, cur.h, pol_a);
-        cur.next(p);
-      }
+      KCursor cur;
+      cur.seek(p, g0 + pro);
       int issued = pro;
       int stage = pro % S;
       uint32_t phase = (pro == S) ? 1u : 0u;
