@@ -42,8 +42,10 @@ namespace {
 
 constexpr int kBlockN = 128;
 constexpr int kBlockK = 128;
-constexpr int kDqGroups = 3;  // dequant warpgroups; group g takes the k-blocks j with j % 3 == g
-constexpr int kThreads = (2 + 4 * kDqGroups) * 32;  // producer, MMA, 3 x 4 dequant warps
+constexpr int kDqGroups = 2;  // dequant warpgroups; group g takes the k-blocks j with j % 2 == g
+constexpr int kEpiWarp0 = 2 + 4 * kDqGroups;        // first of the 4 epilogue warps
+constexpr int kEpiThread0 = kEpiWarp0 * 32;
+constexpr int kThreads = (kEpiWarp0 + 4) * 32;      // producer, MMA, 2 x 4 dequant warps, 4 epilogue warps
 constexpr uint32_t kWTileBytes = kBlockN * kBlockK / 2;  // 8 KiB
 constexpr int kNumABuf = kDqGroups;  // shared-memory A buffer b belongs to dequant group b
 // One dequantized A tile: 128 rows x 128 k of 16-bit values, stored as two
@@ -125,13 +127,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kATileBytes = TN * kBlockK * 2;  // two 128-byte-swizzled boxes of TN x 64
   constexpr uint32_t kBoxBytes = TN * 128;
   constexpr uint32_t kStageBytes = kWTileBytes + kATileBytes;
-  constexpr uint32_t kTmemCols = TN < 32 ? 32 : TN;
+  constexpr uint32_t kAccCols = TN < 32 ? 32 : TN;
+  constexpr uint32_t kTmemCols = 2 * kAccCols;
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
   __shared__ __align__(8) uint64_t aempty_bar[kNumABuf];
-  __shared__ __align__(8) uint64_t tfull_bar, tempty_bar, drain_bar;
+  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], drain_bar;  // accumulators double-buffered
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ int sh_issued, sh_consumed, sh_is_last;
@@ -158,8 +161,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty_bar[s], 5);  // 4 dequant warps + 1 MMA commit
     }
     for (int b = 0; b < kNumABuf; ++b) mbar_init(&aempty_bar[b], 1);
-    mbar_init(&tfull_bar, 1);
-    mbar_init(&tempty_bar, 4);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 4);
+    }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
     sh_issued = 0;
@@ -180,7 +185,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
-  const uint32_t tmem_d = tmem_base;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -238,19 +242,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     // k-block's barrier is reached even after a failed wait, so the dequant
     // warps never wait on a barrier this warp abandoned.
     const uint32_t idesc = idesc_f16_f32(kBlockN, TN, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
-    uint32_t acc_phase = 0;
     int consumed = 0;
     int n_tfull = 0;
     bool bad = false;
     long long g = g0;
     int kb_first = static_cast<int>(g0 % KB);
     int s = 0;
-    while (g < g1) {
+    for (int seg = 0; g < g1; ++seg) {
       const long long seg_len = (KB - kb_first) < (g1 - g) ? (KB - kb_first) : (g1 - g);
       const long long seg_end = g + seg_len;
       kb_first = 0;
-      if (lane == 0 && !bad) bad = !mbar_wait(&tempty_bar, acc_phase ^ 1u, abort_ptr, p.status);
-      acc_phase ^= 1u;
+      // segment `seg` accumulates into accumulator seg % 2, free once the
+      // epilogue drained the segment two back
+      const int acc = seg & 1;
+      const uint32_t tmem_d = tmem_base + acc * kAccCols;
+      if (lane == 0 && !bad)
+        bad = !mbar_wait(&tempty_bar[acc], static_cast<uint32_t>(((seg >> 1) & 1) ^ 1), abort_ptr, p.status);
       for (bool first = true; g < seg_end; ++g, first = false) {
         const int j = static_cast<int>(g - g0);
         const int b = j % kNumABuf;
@@ -273,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++s == S) s = 0;
       }
       if (lane == 0 && !bad) {
-        mma_commit(&tfull_bar);
+        mma_commit(&tfull_bar[acc]);
         ++n_tfull;
       }
       __syncwarp();
@@ -290,11 +297,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
       for (int j = consumed > kNumABuf ? consumed - kNumABuf : 0; j < consumed; ++j)
         mbar_wait(&aempty_bar[j % kNumABuf], static_cast<uint32_t>((j / kNumABuf) & 1), nullptr, p.status);
-      if (n_tfull > 0) mbar_wait(&tfull_bar, static_cast<uint32_t>((n_tfull - 1) & 1), nullptr, p.status);
+      for (int t = n_tfull > 2 ? n_tfull - 2 : 0; t < n_tfull; ++t)
+        mbar_wait(&tfull_bar[t & 1], static_cast<uint32_t>((t >> 1) & 1), nullptr, p.status);
     }
     __syncwarp();
-  } else {
-    // ---------------- dequant warpgroups (warps 2-5: group 0, ..., 14-17: group 3) ----------------
+  } else if (warp < kEpiWarp0) {
+    // ---------------- dequant warpgroups (warps 2-5: group 0, 6-9: group 1) ----------------
     // Control flow stays uniform after an aborted wait (work is skipped, every
     // barrier arrival and named barrier still happens), so no warp is left
     // waiting on a collective that another warp abandoned.
@@ -305,7 +313,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const typename Dq<T>::T2 bias = Dq<T>::bias();
     const bool fold_scale = !p.scale_in_epilogue;
     pdl_wait_primary();
-    uint32_t acc_phase = 0;
     long long g = g0;
     long long tile = g0 / KB;
     int kb0 = static_cast<int>(g0 - tile * KB);
@@ -314,7 +321,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (; g < g1; ++tile, kb0 = 0) {
       const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
       const int kb1 = kb0 + static_cast<int>(seg_len);
-      const bool first_seg = (g == g0);
       int h, nt, mt;
       decode_tile(p, tile, h, nt, mt);
       const int n = nt * kBlockN + row;
@@ -395,9 +401,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar_arrive(kAFullBar0 + b, kAFullCount);
       }
       g += seg_len;
-      if (grp != 0) continue;
-
-      // ---------------- epilogue (group 0) ----------------
+    }
+  } else {
+    // ---------------- epilogue (warps kEpiWarp0 .. kEpiWarp0 + 3) ----------------
+    // Drains accumulator seg % 2 of each segment while the MMA fills the other.
+    // Control flow is uniform across the 128 epilogue threads even after an
+    // aborted wait, so every named barrier is reached by all of them.
+    pdl_wait_primary();
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    long long g = g0;
+    long long tile = g0 / KB;
+    int kb0 = static_cast<int>(g0 - tile * KB);
+    for (int seg = 0; g < g1; ++tile, kb0 = 0, ++seg) {
+      const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
+      const int kb1 = kb0 + static_cast<int>(seg_len);
+      const bool first_seg = (g == g0);
+      g += seg_len;
+      int h, nt, mt;
+      decode_tile(p, tile, h, nt, mt);
+      const int n = nt * kBlockN + row;
+      const int acc = seg & 1;
       const bool whole = (kb0 == 0 && kb1 == KB);
       const int c_first = whole ? 0 : p.sk.owner(tile * KB);
       const int c_last = whole ? 0 : p.sk.owner((tile + 1) * KB - 1);
@@ -409,7 +434,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // The other contributors handled this tile at the start of their ranges;
         // wait (bounded) for all of them and pull their parts in before this
         // CTA's own last MMAs complete.
-        if (threadIdx.x == 64) sh_is_last = wait_counter(&p.counters[c_first], c_last - c_first, abort_ptr, p.status);
+        if (threadIdx.x == kEpiThread0)
+          sh_is_last = wait_counter(&p.counters[c_first], c_last - c_first, abort_ptr, p.status);
         named_bar_sync(1, 128);
         others_ready = sh_is_last != 0;
         if constexpr (kPrefetch) {
@@ -428,12 +454,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      const bool got = mbar_wait(&tfull_bar, acc_phase, abort_ptr, p.status);
-      acc_phase ^= 1u;
+      const bool got = mbar_wait(&tfull_bar[acc], static_cast<uint32_t>((seg >> 1) & 1), abort_ptr, p.status);
       const bool live = __all_sync(0xffffffffu, got);
       tc_fence_after();
       const int m0 = mt * TN;
-      const uint32_t d_addr = tmem_d + lane_off;
+      const uint32_t d_addr = tmem_base + acc * kAccCols + lane_off;
       if (whole) {
         if (live) {
 #pragma unroll 1
@@ -450,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar);
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       } else if (!collect) {
         // Partial tile, not its first contributor: publish this CTA's part.
         const int slot = blockIdx.x * 2 + (first_seg ? 0 : 1);
@@ -468,10 +493,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar);
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
         __threadfence();
         named_bar_sync(1, 128);
-        if (threadIdx.x == 64 && !*abort_ptr) atomicAdd(&p.counters[c_first], 1);
+        if (threadIdx.x == kEpiThread0 && !*abort_ptr) atomicAdd(&p.counters[c_first], 1);
       } else {
         // Partial tile, first contributor: own accumulator + the others' parts.
         if (live && others_ready) {
@@ -501,11 +526,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               emit_row(p, h, n, m0, c * 16, v);
             }
           }
-          if (threadIdx.x == 64) p.counters[c_first] = 0;  // next launch starts from zero
+          if (threadIdx.x == kEpiThread0) p.counters[c_first] = 0;  // next launch starts from zero
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar);
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       }
     }
   }
