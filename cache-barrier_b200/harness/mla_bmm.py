@@ -63,6 +63,15 @@ class Step:
         (self.uk, self.uk_s, self.uk_dq), (self.uv, self.uv_s, self.uv_dq) = make_weights(seed + 1)
         self.k_out = torch.empty(HEADS, self.M, DIM, device=dev, dtype=torch.bfloat16)
         self.v_out = torch.empty(HEADS, self.M, DIM, device=dev, dtype=torch.bfloat16)
+        # fused reconstruction: W_UK | W_UV as one [16, 512, 256] weight (two 128-column
+        # panels per head), output [K_nope | V] = [16, M, 256]; native tiles are per
+        # (head, 128-column panel), so the fused weight interleaves the heads' panels
+        per = self.uk.numel() // HEADS
+        self.ukv = torch.cat([torch.cat([self.uk[h * per:(h + 1) * per], self.uv[h * per:(h + 1) * per]])
+                              for h in range(HEADS)])
+        self.ukv_s = torch.cat([self.uk_s, self.uv_s], dim=2).contiguous()
+        self.ukv_dq = torch.cat([self.uk_dq, self.uv_dq], dim=2).contiguous()
+        self.kv_out = torch.empty(HEADS, self.M, 2 * DIM, device=dev, dtype=torch.bfloat16)
 
     def cb200(self):
         from cb200 import ops
@@ -73,6 +82,14 @@ class Step:
     def cublas(self):
         torch.bmm(self.lat, self.uk_dq, out=self.k_out)
         torch.bmm(self.lat, self.uv_dq, out=self.v_out)
+
+    def cb200_fused(self):
+        from cb200 import ops
+
+        ops.w4a16_gemm(self.lat, self.ukv, self.ukv_s, 2 * DIM, GROUP, out=self.kv_out)
+
+    def cublas_fused(self):
+        torch.bmm(self.lat, self.ukv_dq, out=self.kv_out)
 
     def bytes(self) -> int:
         w = 2 * (HEADS * RANK * DIM // 2 + HEADS * (RANK // GROUP) * DIM * 2)
@@ -128,13 +145,23 @@ def main():
                 rel = st.check()
                 t = graph_time_us(st.cb200, inner=5, reps=15)
                 tc = graph_time_us(st.cublas, inner=5, reps=15)
+                tf = graph_time_us(st.cb200_fused, inner=5, reps=15)
+                tcf = graph_time_us(st.cublas_fused, inner=5, reps=15)
+                st.cb200_fused()
+                torch.cuda.synchronize()
+                ref_f = torch.bmm(st.lat.float(), st.ukv_dq.float())
+                rel_f = ((st.kv_out.float() - ref_f).norm() / ref_f.norm()).item()
+                del ref_f
                 r = {"L": L, "batch": b, "M": st.M, "cb200_us": round(t, 2), "cublas_bf16_us": round(tc, 2),
                      "speedup_vs_cublas": round(tc / t, 3), "rel_err_vs_dequant": round(rel, 5),
+                     "fused_cb200_us": round(tf, 2), "fused_cublas_bf16_us": round(tcf, 2),
+                     "fused_speedup_vs_cublas": round(tcf / tf, 3), "fused_rel_err": round(rel_f, 5),
                      "bytes": st.bytes(), "achieved_gbs": round(st.bytes() / (t * 1e-6) / 1e9, 1),
                      "tflops": round(st.flops() / (t * 1e-6) / 1e12, 1)}
                 rows.append(r)
                 print(f"L={L:5d} b={b:3d} M={st.M:7d}: cb200 {t:9.2f} us ({r['achieved_gbs']} GB/s, "
-                      f"{r['tflops']} TF/s)  cuBLAS {tc:9.2f} us  x{r['speedup_vs_cublas']}  rel {rel:.2e}",
+                      f"{r['tflops']} TF/s)  cuBLAS {tc:9.2f} us  x{r['speedup_vs_cublas']}  rel {rel:.2e} | "
+                      f"fused UK|UV: cb200 {tf:9.2f} cuBLAS {tcf:9.2f} x{r['fused_speedup_vs_cublas']} rel {rel_f:.2e}",
                       flush=True)
                 del st
                 torch.cuda.empty_cache()
