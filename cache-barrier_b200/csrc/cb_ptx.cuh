@@ -73,9 +73,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   const unsigned long long t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
+    if (abort_flag && *abort_flag) return false;
     if (global_timer_ns() - t0 > kWaitLimitNs) {
-      *abort_flag = 1;
+      if (abort_flag) *abort_flag = 1;
       if (status) atomicOr(status, CB_DEVERR_TIMEOUT);
       return false;
     }

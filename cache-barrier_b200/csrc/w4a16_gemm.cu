@@ -289,16 +289,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       sh_consumed = consumed;
       mma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, nullptr, p.status);
-      // Every commit arrival this thread issued must land before the CTA exits
-      // (an arrive on released shared memory faults): the releases of the last
-      // S stages, of the last use of each TMEM A buffer, and the last
-      // accumulator hand-off.
-      for (int j = consumed > S ? consumed - S : 0; j < consumed; ++j)
-        mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
-      for (int j = consumed > kNumABuf ? consumed - kNumABuf : 0; j < consumed; ++j)
-        mbar_wait(&aempty_bar[j % kNumABuf], static_cast<uint32_t>((j / kNumABuf) & 1), nullptr, p.status);
-      for (int t = n_tfull > 2 ? n_tfull - 2 : 0; t < n_tfull; ++t)
-        mbar_wait(&tfull_bar[t & 1], static_cast<uint32_t>((t >> 1) & 1), nullptr, p.status);
+    }
+    // Every commit arrival lane 0 issued must land before the CTA exits (an
+    // arrive on released shared memory faults): the releases of the last S
+    // stages, of the last use of each A buffer, and the last accumulator
+    // hand-offs. One lane per barrier, so the waits overlap.
+    consumed = __shfl_sync(0xffffffffu, consumed, 0);
+    n_tfull = __shfl_sync(0xffffffffu, n_tfull, 0);
+    {
+      const int j = consumed - 1 - lane;
+      if (lane < S && j >= 0) mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
+      const int ja = consumed - 1 - (lane - 24);  // lanes 24.. : A-buffer releases
+      if (lane >= 24 && lane < 24 + kNumABuf && ja >= 0)
+        mbar_wait(&aempty_bar[ja % kNumABuf], static_cast<uint32_t>((ja / kNumABuf) & 1), nullptr, p.status);
+      const int t = n_tfull - 1 - (lane - 30);  // lanes 30, 31: the last two accumulator hand-offs
+      if (lane >= 30 && t >= 0) mbar_wait(&tfull_bar[t & 1], static_cast<uint32_t>((t >> 1) & 1), nullptr, p.status);
     }
     __syncwarp();
   } else if (warp < kEpiWarp0) {

@@ -242,11 +242,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       sh_consumed = consumed;
       mma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, nullptr, p.status);
-      // every commit arrival must land before the CTA exits
-      for (int j = consumed > S ? consumed - S : 0; j < consumed; ++j)
-        mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
-      for (int t = tiles > 2 ? tiles - 2 : 0; t < tiles; ++t)
-        mbar_wait(&acc_full[t & 1], static_cast<uint32_t>((t >> 1) & 1), nullptr, p.status);
+    }
+    // every commit arrival lane 0 issued must land before the CTA exits; one
+    // lane per barrier so the waits overlap
+    consumed = __shfl_sync(0xffffffffu, consumed, 0);
+    tiles = __shfl_sync(0xffffffffu, tiles, 0);
+    {
+      const int j = consumed - 1 - lane;
+      if (lane < S && j >= 0) mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
+      const int t = tiles - 1 - (lane - 30);
+      if (lane >= 30 && t >= 0) mbar_wait(&acc_full[t & 1], static_cast<uint32_t>((t >> 1) & 1), nullptr, p.status);
     }
     __syncwarp();
   } else if (warp == kWaiterWarp) {

@@ -89,6 +89,23 @@ __device__ __forceinline__ void emit_row(const Params& p, int h, int n, int m0, 
   }
 }
 
+// emit_row with the scales already in registers (loaded when the segment began).
+__device__ __forceinline__ void emit_row_pre(const Params& p, int h, int n, int m0, int t0, const int32_t (&v)[16],
+                                             float ws, const float (&as)[16]) {
+  if (n >= p.N) return;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int m = m0 + t0 + j;
+    if (m < p.M) {
+      const long long idx = h * p.out_sb + static_cast<long long>(m) * p.out_sm + n;
+      float f = __int2float_rn(v[j]);
+      if (!p.raw_f32) f = __fmul_rn(__fmul_rn(f, as[j]), ws);
+      store_elem(p.out, p.out_dtype, idx, f);
+      if (p.acc_out) p.acc_out[idx] = v[j];
+    }
+  }
+}
+
 // Adds the published parts of contributors [c_lo, c_hi] (each its first
 // segment, slot kind 0) for chunk c of this thread's row; loads of four
 // contributors are in flight together.
@@ -274,12 +291,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       // All issued MMAs must finish before TMEM is released.
       mma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, nullptr, p.status);
-      // Every commit arrival this thread issued must land before the CTA exits
-      // (an arrive on released shared memory faults): the releases of the last
-      // S stages and the last accumulator hand-off.
-      for (int j = consumed > S ? consumed - S : 0; j < consumed; ++j)
-        mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
-      if (n_tfull > 0) mbar_wait(&tfull_bar, static_cast<uint32_t>((n_tfull - 1) & 1), nullptr, p.status);
+    }
+    // Every commit arrival lane 0 issued must land before the CTA exits (an
+    // arrive on released shared memory faults): the releases of the last S
+    // stages and the last accumulator hand-off. One lane per barrier, so the
+    // waits overlap instead of adding up.
+    consumed = __shfl_sync(0xffffffffu, consumed, 0);
+    n_tfull = __shfl_sync(0xffffffffu, n_tfull, 0);
+    {
+      const int j = consumed - 1 - lane;  // lane l waits the (l+1)-th most recent stage release
+      if (lane < S && j >= 0) mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
+      if (lane == 31 && n_tfull > 0)
+        mbar_wait(&tfull_bar, static_cast<uint32_t>((n_tfull - 1) & 1), nullptr, p.status);
     }
     __syncwarp();
   } else if (warp == kWaiterWarp) {
@@ -322,6 +345,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int c_last = whole ? 0 : p.sk.owner((tile + 1) * KB - 1);
       const bool collect = !whole && static_cast<int>(blockIdx.x) == c_first;
       constexpr bool kPrefetch = TN <= 32;
+      int h, nt, mt;
+      decode_tile(p, tile, h, nt, mt);
+      const int n = nt * kBlockN + row;
+      const int m0 = mt * TN;
+      // Scales of the rows this segment stores, loaded before any wait so the
+      // stores after the last MMA depend on nothing in flight.
+      float ws_pre = 1.0f;
+      float as_pre[kPrefetch ? TN : 1];
+      if constexpr (kPrefetch) {
+        const bool stores = whole || collect;
+#pragma unroll
+        for (int j = 0; j < TN; ++j)
+          as_pre[j] = (stores && !p.raw_f32 && m0 + j < p.M) ? __ldg(p.a_scale + h * p.as_sb + m0 + j) : 1.0f;
+        if (stores && !p.raw_f32 && n < p.N) ws_pre = __ldg(p.w_scale + h * p.ws_sb + n);
+      }
       int32_t other[kPrefetch ? TN : 1];
       bool others_ready = true;
       if (collect) {
@@ -351,23 +389,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc_phase ^= 1u;
       const bool live = __all_sync(0xffffffffu, got);
       tc_fence_after();
-      int h, nt, mt;
-      decode_tile(p, tile, h, nt, mt);
-      const int n = nt * kBlockN + row;
-      const int m0 = mt * TN;
       if (whole) {
         // Whole tile in this CTA: epilogue straight from TMEM.
         if (live) {
-#pragma unroll 1
-          for (int c = 0; c < TN / 16; ++c) {
-            uint32_t r[16];
-            __syncwarp();
-            tmem_ld16(lane_addr + c * 16, r);
-            tmem_ld_wait();
-            int32_t v[16];
+          if constexpr (kPrefetch) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = static_cast<int32_t>(r[j]);
-            emit_row<TN>(p, h, n, m0, c * 16, v);
+            for (int c = 0; c < TN / 16; ++c) {
+              uint32_t r[16];
+              __syncwarp();
+              tmem_ld16(lane_addr + c * 16, r);
+              tmem_ld_wait();
+              int32_t v[16];
+              float as16[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                v[j] = static_cast<int32_t>(r[j]);
+                as16[j] = as_pre[c * 16 + j];
+              }
+              emit_row_pre(p, h, n, m0, c * 16, v, ws_pre, as16);
+            }
+          } else {
+#pragma unroll 1
+            for (int c = 0; c < TN / 16; ++c) {
+              uint32_t r[16];
+              __syncwarp();
+              tmem_ld16(lane_addr + c * 16, r);
+              tmem_ld_wait();
+              int32_t v[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = static_cast<int32_t>(r[j]);
+              emit_row<TN>(p, h, n, m0, c * 16, v);
+            }
           }
         }
         tc_fence_before();
@@ -407,9 +459,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               tmem_ld16(lane_addr + c * 16, r);
               tmem_ld_wait();
               int32_t v[16];
+              float as16[16];
 #pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] = static_cast<int32_t>(r[j]) + other[c * 16 + j];
-              emit_row<TN>(p, h, n, m0, c * 16, v);
+              for (int j = 0; j < 16; ++j) {
+                v[j] = static_cast<int32_t>(r[j]) + other[c * 16 + j];
+                as16[j] = as_pre[c * 16 + j];
+              }
+              emit_row_pre(p, h, n, m0, c * 16, v, ws_pre, as16);
             }
           } else {
 #pragma unroll 1
