@@ -457,6 +457,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 16; ++j) other[c * 16 + j] = v[j];
             }
           }
+          // Complete the partial sums now, while this CTA's last MMAs run; the
+          // compiler would otherwise sink the loads to their use after the wait.
+#pragma unroll
+          for (int j = 0; j < TN; ++j) asm volatile("" ::"f"(other[j]));
         }
       }
       const bool got = mbar_wait(&tfull_bar[acc], static_cast<uint32_t>((seg >> 1) & 1), abort_ptr, p.status);

@@ -359,6 +359,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < TN; ++j)
           as_pre[j] = (stores && !p.raw_f32 && m0 + j < p.M) ? __ldg(p.a_scale + h * p.as_sb + m0 + j) : 1.0f;
         if (stores && !p.raw_f32 && n < p.N) ws_pre = __ldg(p.w_scale + h * p.ws_sb + n);
+        // Consume the values here, so the compiler cannot sink the loads to
+        // their use after the last MMA.
+#pragma unroll
+        for (int j = 0; j < TN; ++j) asm volatile("" ::"f"(as_pre[j]));
+        asm volatile("" ::"f"(ws_pre));
       }
       int32_t other[kPrefetch ? TN : 1];
       bool others_ready = true;
@@ -383,6 +388,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 16; ++j) other[c * 16 + j] = v[j];
             }
           }
+          // Complete the partial sums now, while this CTA's last MMAs run; the
+          // compiler would otherwise sink the loads to their use after the wait.
+#pragma unroll
+          for (int j = 0; j < TN; ++j) asm volatile("" ::"r"(other[j]));
         }
       }
       const bool got = mbar_wait(&tfull_bar, acc_phase, abort_ptr, p.status);
