@@ -37,6 +37,7 @@ CB_DTYPE_I32 = 5
 CB_OP_W8A8 = 0
 CB_OP_W4A16 = 1
 CB_OP_W4A4 = 2
+CB_OP_NVFP4 = 3
 
 # W4A4 nibble modes
 CB_W4A4_SIGNED = 0
@@ -67,6 +68,9 @@ SIGNATURES = {
     "cb_w4a16_gemm": (_int, [_vp, _int, _vp, _vp, _int, _i64, _vp, _int, _i64, _i64, _i64, _i64, _vp, _vp, _sz,
                              _vp]),
     "cb_w4a4_gemm": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _int, _vp, _sz, _vp]),
+    "cb_nvfp4_quantize": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
+    "cb_nvfp4_gemm": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz,
+                             _vp]),
     "cb_repack_w4": (_int, [_vp, _int, _vp, _i64, _i64, _i64, _vp]),
     "cb_w4_native_bytes": (_sz, [_i64, _i64, _i64]),
     "cb_repack_w8_kmajor": (_int, [_vp, _vp, _i64, _i64, _i64, _vp]),

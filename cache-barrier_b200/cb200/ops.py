@@ -362,6 +362,69 @@ def w4a4_gemm(a_packed: torch.Tensor, b_packed: torch.Tensor, K: int, out: torch
     return out
 
 
+# ---------------------------------------------------------------------------
+# NVFP4 (e2m1 values, e4m3 scales per 16 elements; vLLM's tensor formats)
+# ---------------------------------------------------------------------------
+def nvfp4_scale_shape(rows: int, K: int) -> tuple[int, int]:
+    """Shape of the swizzled scale tensor: rows padded to 128, K/16 to 4."""
+    return (-(-rows // 128) * 128, -(-(K // 16) // 4) * 4)
+
+
+def nvfp4_quantize(x: torch.Tensor, global_scale: torch.Tensor, q: torch.Tensor | None = None,
+                   sf: torch.Tensor | None = None):
+    """``x`` [rows, K] f16/bf16 -> (packed e2m1 uint8 [rows, K/2], swizzled e4m3
+    scales uint8 ``nvfp4_scale_shape(rows, K)``), with ``global_scale`` one fp32
+    on the device (vLLM's ``scaled_fp4_quant(x, global_scale)``)."""
+    _require_cuda(x, global_scale, q, sf)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be [rows, K] with contiguous rows")
+    rows, K = x.shape
+    if global_scale.dtype != torch.float32 or global_scale.numel() != 1:
+        raise ValueError("global_scale must be one fp32 value")
+    if q is None:
+        q = torch.empty((rows, K // 2), dtype=torch.uint8, device=x.device)
+    if sf is None:
+        sf = torch.empty(nvfp4_scale_shape(rows, K), dtype=torch.uint8, device=x.device)
+    if q.dtype != torch.uint8 or sf.dtype != torch.uint8 or not sf.is_contiguous():
+        raise ValueError("q and sf must be uint8, sf contiguous")
+    if sf.numel() < nvfp4_scale_shape(rows, K)[0] * nvfp4_scale_shape(rows, K)[1]:
+        raise ValueError("sf is too small")
+    code = L.load().cb_nvfp4_quantize(x.data_ptr(), dtype_code(x.dtype), rows, K, x.stride(0),
+                                      global_scale.data_ptr(), q.data_ptr(), q.stride(0), sf.data_ptr(),
+                                      _stream(x.device))
+    L.check("cb_nvfp4_quantize", code)
+    return q, sf
+
+
+def nvfp4_gemm(a: torch.Tensor, a_sf: torch.Tensor, b: torch.Tensor, b_sf: torch.Tensor, alpha: torch.Tensor,
+               out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``out[m, n] = alpha * A[m] . B[n]`` for packed NVFP4 activations ``a``
+    [M, K/2] and weights ``b`` [N, K/2] with their swizzled scales (vLLM's
+    ``cutlass_scaled_fp4_mm(a, b, a_sf, b_sf, alpha, out_dtype)``)."""
+    _require_cuda(a, a_sf, b, b_sf, alpha, out)
+    if a.dtype != torch.uint8 or b.dtype != torch.uint8 or a.dim() != 2 or b.dim() != 2:
+        raise ValueError("a and b must be packed uint8 [rows, K/2]")
+    M, K = a.shape[0], a.shape[1] * 2
+    N = b.shape[0]
+    if b.shape[1] * 2 != K:
+        raise ValueError("a and b disagree on K")
+    if a.stride(1) != 1 or b.stride(1) != 1 or not a_sf.is_contiguous() or not b_sf.is_contiguous():
+        raise ValueError("operands must have contiguous rows and contiguous scales")
+    if alpha.dtype != torch.float32 or alpha.numel() != 1:
+        raise ValueError("alpha must be one fp32 value")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    if out.shape != (M, N) or out.stride(1) != 1:
+        raise ValueError("out must be [M, N] contiguous along N")
+    nbytes = workspace_bytes(L.CB_OP_NVFP4, 1, M, N, K)
+    ws = POOL.get(nbytes, a.device)
+    code = L.load().cb_nvfp4_gemm(a.data_ptr(), a_sf.data_ptr(), b.data_ptr(), b_sf.data_ptr(), alpha.data_ptr(),
+                                  out.data_ptr(), dtype_code(out.dtype), M, N, K, a.stride(0), b.stride(0),
+                                  out.stride(0), ws.data_ptr(), ws.numel(), _stream(a.device))
+    L.check("cb_nvfp4_gemm", code)
+    return out
+
+
 def device_status(device: torch.device | None = None) -> int:
     """Synchronising check of the kernels' device-side status words (0 = no timeout)."""
     return POOL.check_status(device)

@@ -249,6 +249,8 @@ size_t cb_workspace_bytes(int op, int64_t batch, int64_t M, int64_t N, int64_t K
       return w8a8_workspace_bytes(batch, M, N, K);
     case CB_OP_W4A16:
       return w4a16_workspace_bytes(batch, M, N, K);
+    case CB_OP_NVFP4:
+      return nvfp4_workspace_bytes(M);
     case CB_OP_W4A4: {
       // the int8 GEMM scratch, then unpacked A [M, K] and B [N, K] (8-bit).
       const size_t a = align_up(static_cast<size_t>(M) * K, 256);
@@ -394,6 +396,53 @@ int cb_w4a16_gemm(const void* a, int a_dtype, const uint8_t* w_native, const voi
   L.workspace = workspace;
   L.workspace_bytes = workspace_bytes;
   return launch_w4a16(L, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int cb_nvfp4_quantize(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t x_stride, const float* global_scale,
+                      uint8_t* q, int64_t q_stride, uint8_t* sf, cb_stream_t stream) {
+  if (rows < 0 || K < 0) return CB_ERR_INVALID_ARG;
+  if (rows == 0 || K == 0) return CB_OK;
+  if (!x || !global_scale || !q || !sf) return CB_ERR_INVALID_ARG;
+  if (x_dtype != CB_DTYPE_BF16 && x_dtype != CB_DTYPE_F16) return CB_ERR_DTYPE;
+  if (K % 64 != 0) return CB_ERR_SHAPE;
+  if (rows > 0x7fffffffLL || K > 0x7fffffffLL) return CB_ERR_TOO_LARGE;
+  if (x_stride < K || q_stride < K / 2) return CB_ERR_STRIDE;
+  if (!aligned16(x) || x_stride % 8 != 0 || reinterpret_cast<uintptr_t>(q) % 8 != 0 || q_stride % 8 != 0)
+    return CB_ERR_ALIGNMENT;
+  return launch_nvfp4_quant(x, x_dtype, rows, K, x_stride, global_scale, q, q_stride, sf,
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+int cb_nvfp4_gemm(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, const float* alpha,
+                  void* out, int out_dtype, int64_t M, int64_t N, int64_t K, int64_t a_stride, int64_t b_stride,
+                  int64_t out_stride, void* workspace, size_t workspace_bytes, cb_stream_t stream) {
+  if (M < 0 || N < 0 || K < 0) return CB_ERR_INVALID_ARG;
+  if (M * N == 0) return CB_OK;
+  if (!a || !a_sf || !b || !b_sf || !alpha || !out) return CB_ERR_INVALID_ARG;
+  if (!valid_out_dtype(out_dtype)) return CB_ERR_DTYPE;
+  if (K == 0 || K % 64 != 0) return CB_ERR_SHAPE;
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL) return CB_ERR_TOO_LARGE;
+  if (a_stride < K / 2 || b_stride < K / 2 || out_stride < N) return CB_ERR_STRIDE;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(a_sf) || !aligned16(b_sf) || a_stride % 16 != 0 ||
+      b_stride % 16 != 0)
+    return CB_ERR_ALIGNMENT;
+  Nvfp4Launch L = {};
+  L.a = a;
+  L.a_sf = a_sf;
+  L.b = b;
+  L.b_sf = b_sf;
+  L.alpha = alpha;
+  L.out = out;
+  L.out_dtype = out_dtype;
+  L.M = M;
+  L.N = N;
+  L.K = K;
+  L.a_sm = a_stride;
+  L.b_sn = b_stride;
+  L.out_sm = out_stride;
+  L.workspace = workspace;
+  L.workspace_bytes = workspace_bytes;
+  return launch_nvfp4_gemm(L, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int cb_w4a4_gemm(const uint8_t* a_packed, const uint8_t* b_packed, float* c, int64_t M, int64_t N, int64_t K,

@@ -110,4 +110,25 @@ bool w4a16_resident_eligible(const W4A16Launch& L);
 int launch_w4a16_resident(const W4A16Launch& L, cudaStream_t stream);
 size_t w4a16_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K);
 
+// NVFP4 GEMM: out[M, N] = alpha * A[M, K] . B[N, K]^T (nvfp4.cu). a/b: packed
+// e2m1 [rows, K/2] with row strides a_sm / b_sn in bytes; a_sf / b_sf: swizzled
+// e4m3 scale atoms; alpha: one fp32 on the device.
+struct Nvfp4Launch {
+  const uint8_t* a;
+  const uint8_t* a_sf;
+  const uint8_t* b;
+  const uint8_t* b_sf;
+  const float* alpha;
+  void* out;
+  int out_dtype;
+  int64_t M, N, K;
+  int64_t a_sm, b_sn, out_sm;
+  void* workspace;
+  size_t workspace_bytes;
+};
+int launch_nvfp4_gemm(const Nvfp4Launch& L, cudaStream_t stream);
+int launch_nvfp4_quant(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t x_sm, const float* global_scale,
+                       uint8_t* q, int64_t q_sm, uint8_t* sf, cudaStream_t stream);
+size_t nvfp4_workspace_bytes(int64_t M);
+
 }  // namespace cb

@@ -22,6 +22,10 @@ call shapes for the int8 W8A8 and int4 W4A16 paths:
   apply_w4a16_linear(x, w_native, scales, N, K, bias=None)
       x [M, K] @ dequant(w)^T -> [M, N] in x's dtype; takes the place of
       apply_fp8_marlin_linear(x, qw, s, workspace, N, K, None).
+  scaled_fp4_quant(x, global_scale) -> (q uint8 [M, K/2], scales e4m3 [pad(M,128), pad(K/16,4)])
+  cutlass_scaled_fp4_mm(a, b, block_scale_a, block_scale_b, alpha, out_dtype)
+      NVFP4 in vLLM's call shapes and tensor formats (the reference's native-FP4
+      path, profiling/cuda_validation/bench_moe_nvfp4_native.py:97-108).
 """
 
 from __future__ import annotations
@@ -107,3 +111,19 @@ def apply_w4a16_linear(x: torch.Tensor, w_native: torch.Tensor, scales: torch.Te
     if bias is not None:
         y += bias.to(y.dtype)
     return y.reshape(*x.shape[:-1], N)
+
+
+def scaled_fp4_quant(x: torch.Tensor, input_global_scale: torch.Tensor):
+    """NVFP4 quantization of ``x`` [M, K] (vLLM ``scaled_fp4_quant``): packed e2m1
+    values uint8 [M, K/2] and the swizzled e4m3 scales, viewed as float8_e4m3fn
+    [pad(M, 128), pad(K/16, 4)]."""
+    q, sf = ops.nvfp4_quantize(x, input_global_scale.reshape(1).to(torch.float32))
+    return q, sf.view(torch.float8_e4m3fn)
+
+
+def cutlass_scaled_fp4_mm(a: torch.Tensor, b: torch.Tensor, block_scale_a: torch.Tensor, block_scale_b: torch.Tensor,
+                          alpha: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
+    """``alpha * A @ B^T`` for NVFP4 ``a`` [M, K/2] and ``b`` [N, K/2] with their
+    swizzled scales (vLLM ``cutlass_scaled_fp4_mm``)."""
+    return ops.nvfp4_gemm(a, block_scale_a.view(torch.uint8), b, block_scale_b.view(torch.uint8),
+                          alpha.reshape(1).to(torch.float32), out_dtype=out_dtype)

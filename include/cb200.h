@@ -62,7 +62,7 @@ enum cb_dtype {
 };
 
 /* ---- operation codes (for cb_workspace_bytes) --------------------------- */
-enum cb_op { CB_OP_W8A8 = 0, CB_OP_W4A16 = 1, CB_OP_W4A4 = 2 };
+enum cb_op { CB_OP_W8A8 = 0, CB_OP_W4A16 = 1, CB_OP_W4A4 = 2, CB_OP_NVFP4 = 3 };
 
 /* ---- int4 weight layouts ------------------------------------------------ */
 enum cb_w4_layout {
@@ -184,6 +184,39 @@ enum cb_w4a4_mode {
 CB_API int cb_w4a4_gemm(const uint8_t* a_packed, const uint8_t* b_packed, float* c, int64_t M, int64_t N, int64_t K,
                         int64_t lda, int64_t ldb, int64_t ldc, int nibble_mode, void* workspace,
                         size_t workspace_bytes, cb_stream_t stream);
+
+/* ---- NVFP4 (e2m1 values, e4m3 scales per 16 elements) ------------------- */
+/* The matched-precision W4A4 path the reference runs through vLLM on B200
+   (profiling/cuda_validation/bench_moe_nvfp4_native.py:97-108: scaled_fp4_quant,
+   run_cutlass_moe_fp4), in vLLM's tensor formats (vllm 0.22.0):
+     values: uint8 [rows, K/2], element 2i in the low nibble, 2i+1 in the high;
+             nibble = sign << 3 | index into {0, 0.5, 1, 1.5, 2, 3, 4, 6};
+     scales: e4m3 bytes, 512-byte atoms of 128 rows x 4 scale columns,
+             ceil(rows/128) * ceil(K/64) atoms, byte (r, c) at
+             ((r/128) * ceil(K/64) + c/4) * 512 + (r%32) * 16 + ((r%128)/32) * 4 + c%4.
+   Quantization of x [rows, K] (f16 / bf16, row stride x_stride elements) with a
+   per-tensor global scale gs (one fp32 on the device), as vLLM's
+   ref_nvfp4_quant (nvfp4_emulation_utils.py:439-453):
+     s = e4m3(gs * amax_block * (1/6)), o = 1 / (s * (1/gs)), q = e2m1(clamp(x * o, +-6)),
+   round to nearest even throughout; padding scale bytes are written as 0.
+   q: [rows, K/2] with row stride q_stride bytes; sf: ceil(rows/128)*128 * K/16 bytes
+   (K % 64 == 0). Replaces vllm._custom_ops.scaled_fp4_quant(x, gs). */
+CB_API int cb_nvfp4_quantize(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t x_stride,
+                             const float* global_scale, uint8_t* q, int64_t q_stride, uint8_t* sf,
+                             cb_stream_t stream);
+/* out[m, n] = alpha * sum_k A[m, k] * B[n, k], fp32 accumulation on the
+   tensor cores' block-scaled FP4 path (tcgen05.mma kind::mxf4nvf4).
+   a: activations [M, K/2] (row stride a_stride bytes), a_sf their scales;
+   b: weights [N, K/2] (row stride b_stride bytes), b_sf their scales;
+   alpha: one fp32 on the device (1 / (gs_a * gs_b) for vLLM-quantized operands);
+   out: [M, N] f16 / bf16 / f32, row stride out_stride elements. K % 64 == 0;
+   16-byte aligned operands and strides. Workspace from
+   cb_workspace_bytes(CB_OP_NVFP4, 1, M, N, K). Replaces
+   vllm._custom_ops.cutlass_scaled_fp4_mm(a, b, a_sf, b_sf, alpha, out_dtype). */
+CB_API int cb_nvfp4_gemm(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf,
+                         const float* alpha, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                         int64_t a_stride, int64_t b_stride, int64_t out_stride, void* workspace,
+                         size_t workspace_bytes, cb_stream_t stream);
 
 /* ---- weight preparation (offline, device-side) -------------------------- */
 /* Repack int4 weights from CB_W4_REF_U8_KN or CB_W4_I32_K8N into CB_W4_NATIVE.

@@ -308,3 +308,120 @@ def rmsnorm_quant_i8(x_bits_or_f32, weight_f32, eps, dtype="bf16"):
     y = bf16_bits_to_f32(f32_to_bf16_bits(yf)) if dtype == "bf16" else yf.astype(np.float16).astype(np.float32)
     q, s = quant_act_i8(y)
     return q, s, y
+
+
+# ---------------------------------------------------------------------------
+# NVFP4 (e2m1 values, e4m3 block scales per 16 elements).
+# The reference runs this path through vLLM (profiling/cuda_validation/
+# bench_moe_nvfp4_native.py:97-108); its arithmetic is vLLM 0.22.0's
+# ref_nvfp4_quant / cast_to_fp4 / dequantize_to_dtype
+# (vllm/model_executor/layers/quantization/utils/nvfp4_emulation_utils.py:
+# 328-453) and the swizzled scale layout of its convert_swizzled_to_linear
+# (:348-355). Pinned in tests/test_oracle_golden.py against fixtures made by
+# running those vLLM functions on the CPU (tests/golden/make_golden_nvfp4.py).
+# ---------------------------------------------------------------------------
+
+E2M1_VALUES = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], dtype=np.float32)
+
+
+def e4m3_round(x) -> tuple[np.ndarray, np.ndarray]:
+    """Non-negative fp32 -> e4m3 (finite, max 448), round to nearest even.
+    Returns (bits uint8, value float32)."""
+    x = np.minimum(np.asarray(x, dtype=np.float64), 448.0)
+    e = np.floor(np.log2(np.maximum(x, 2.0 ** -9)))
+    e = np.maximum(e, -6.0)  # subnormals share the exponent of 2^-6
+    quantum = np.exp2(e - 3.0)
+    v = np.rint(x / quantum) * quantum  # exact: x / quantum and the product are exact in float64
+    v = np.minimum(v, 448.0)
+    ev = np.floor(np.log2(np.maximum(v, 2.0 ** -9)))
+    normal = v >= 2.0 ** -6
+    exp_field = np.where(normal, ev + 7.0, 0.0)
+    mant = np.where(normal, v / np.exp2(ev) * 8.0 - 8.0, v / 2.0 ** -9)
+    bits = np.where(v == 0, 0, exp_field * 8 + mant).astype(np.uint8)
+    return bits, v.astype(np.float32)
+
+
+def e4m3_bits_to_f32(b) -> np.ndarray:
+    b = np.asarray(b, dtype=np.uint8).astype(np.int64)
+    sign = np.where(b & 0x80, -1.0, 1.0)
+    exp_field = (b >> 3) & 0xF
+    mant = b & 0x7
+    v = np.where(exp_field == 0, mant * 2.0 ** -9, (1.0 + mant / 8.0) * np.exp2(exp_field - 7.0))
+    return (sign * v).astype(np.float32)
+
+
+def e2m1_nibbles(y: np.ndarray) -> np.ndarray:
+    """fp32 in [-6, 6] -> e2m1 nibble (cast_to_fp4's thresholds, round to nearest
+    even; the sign bit follows y's sign, so negative values that round to 0 give 0x8)."""
+    y = np.asarray(y, dtype=np.float32)
+    a = np.abs(y)
+    m = np.select([a <= 0.25, a < 0.75, a <= 1.25, a < 1.75, a <= 2.5, a < 3.5, a <= 5.0], [0, 1, 2, 3, 4, 5, 6], 7)
+    sign = np.signbit(y).astype(np.int64) << 3
+    return (sign | m).astype(np.uint8)
+
+
+def e2m1_to_f32(nib: np.ndarray) -> np.ndarray:
+    nib = np.asarray(nib, dtype=np.uint8)
+    v = E2M1_VALUES[nib & 7]
+    return np.where(nib & 8, -v, v).astype(np.float32)
+
+
+def nvfp4_quant(x_f32: np.ndarray, global_scale: float):
+    """ref_nvfp4_quant (nvfp4_emulation_utils.py:439-453) on [rows, K] fp32 inputs
+    (exact values of the 16-bit activations). Returns (packed uint8 [rows, K/2],
+    scale bits uint8 [rows, K/16] in row-major order, nibbles uint8 [rows, K])."""
+    x = np.asarray(x_f32, dtype=np.float32)
+    rows, K = x.shape
+    gs = np.float32(global_scale)
+    blocks = x.reshape(rows, K // 16, 16)
+    vmax = np.max(np.abs(blocks), axis=-1).astype(np.float32)
+    s = (gs * (vmax * np.float32(1.0 / 6.0)).astype(np.float32)).astype(np.float32)
+    s = np.clip(s, -448.0, 448.0).astype(np.float32)
+    s_bits, s_val = e4m3_round(s)
+    rgs = np.float32(1.0) / (gs + np.float32(1e8) * np.float32(gs == 0))
+    t = (s_val * rgs).astype(np.float32)
+    o = (np.float32(1.0) / (t + np.float32(1e8) * (t == 0).astype(np.float32))).astype(np.float32)
+    y = np.clip((blocks * o[..., None]).astype(np.float32), -6.0, 6.0).reshape(rows, K)
+    nib = e2m1_nibbles(y)
+    packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).astype(np.uint8)
+    return packed, s_bits, nib
+
+
+def nvfp4_swizzle(sf_rows_cols: np.ndarray) -> np.ndarray:
+    """Row-major scale bytes [rows, C] -> the swizzled atom layout, zero padded to
+    [ceil(rows/128)*128, ceil(C/4)*4] (inverse of convert_swizzled_to_linear)."""
+    sf = np.asarray(sf_rows_cols, dtype=np.uint8)
+    rows, C = sf.shape
+    rp, cp = -(-rows // 128) * 128, -(-C // 4) * 4
+    full = np.zeros((rp, cp), dtype=np.uint8)
+    full[:rows, :C] = sf
+    # [m_tiles, 4 (i4), 32 (i3), k_tiles, 4 (i5)] -> [m_tiles, k_tiles, 32, 4, 4]
+    t = full.reshape(rp // 128, 4, 32, cp // 4, 4).transpose(0, 3, 2, 1, 4)
+    return np.ascontiguousarray(t).reshape(-1)
+
+
+def nvfp4_unswizzle(buf: np.ndarray, rows: int, K: int) -> np.ndarray:
+    C = K // 16
+    rp, cp = -(-rows // 128) * 128, -(-C // 4) * 4
+    t = np.asarray(buf, dtype=np.uint8)[: rp * cp].reshape(rp // 128, cp // 4, 32, 4, 4).transpose(0, 3, 2, 1, 4)
+    return np.ascontiguousarray(t).reshape(rp, cp)[:rows, :C]
+
+
+def nvfp4_dequant(packed: np.ndarray, sf_bits: np.ndarray) -> np.ndarray:
+    """float64 values e2m1 * e4m3 of [rows, K/2] packed values and [rows, K/16]
+    row-major scale bits (no global scale)."""
+    p = np.asarray(packed, dtype=np.uint8)
+    rows = p.shape[0]
+    nib = np.empty((rows, p.shape[1] * 2), dtype=np.uint8)
+    nib[:, 0::2] = p & 0xF
+    nib[:, 1::2] = p >> 4
+    v = e2m1_to_f32(nib).astype(np.float64).reshape(rows, -1, 16)
+    return (v * e4m3_bits_to_f32(sf_bits).astype(np.float64)[..., None]).reshape(rows, -1)
+
+
+def nvfp4_gemm(a_packed, a_sf_bits, b_packed, b_sf_bits, alpha: float) -> np.ndarray:
+    """out[m, n] = alpha * sum_k A[m, k] B[n, k] in float64 (exact products; the
+    kernel accumulates in fp32), returned as float64."""
+    A = nvfp4_dequant(a_packed, a_sf_bits)
+    B = nvfp4_dequant(b_packed, b_sf_bits)
+    return (A @ B.T) * np.float64(np.float32(alpha))

@@ -103,3 +103,48 @@ def test_bf16_rounding_helper():
     assert list(b[:4]) == [0x3F80, 0x3F80, 0x3F81, 0xC020]
     back = O.bf16_bits_to_f32(b)
     assert np.all(np.abs(back - x) <= np.abs(x) * 2.0 ** -8)
+
+
+@pytest.mark.parametrize("name", ["bf16_r5_k256_amax", "f16_r3_k128_g1", "bf16_r130_k64_g37"])
+def test_nvfp4_quant_matches_vllm_reference(golden, name):
+    """Values and scales of vLLM's ref_nvfp4_quant (the arithmetic of the reference's
+    native-FP4 path), reproduced exactly."""
+    d = golden(f"nvfp4_quant_{name}.npz")
+    x = O.bf16_bits_to_f32(d["x_bits"]) if bool(d["x_is_bf16"]) else d["x_bits"].view(np.float16).astype(np.float32)
+    packed, s_bits, nib = O.nvfp4_quant(x, float(d["gs"]))
+    assert np.array_equal(O.e2m1_to_f32(nib), d["q_values"])
+    assert np.array_equal(O.e4m3_bits_to_f32(s_bits), d["scales"])
+    # the packed bytes hold element 2i in the low nibble
+    assert np.array_equal(packed & 0xF, nib[:, 0::2]) and np.array_equal(packed >> 4, nib[:, 1::2])
+
+
+def test_nvfp4_swizzle_matches_vllm_layout(golden):
+    d = golden("nvfp4_swizzle.npz")
+    rows, K = int(d["rows"]), int(d["K"])
+    assert np.array_equal(O.nvfp4_unswizzle(d["swizzled"], rows, K), d["linear"])
+    again = O.nvfp4_unswizzle(O.nvfp4_swizzle(d["linear"]), rows, K)
+    assert np.array_equal(again, d["linear"])
+
+
+def test_e4m3_rounding_matches_torch_float8():
+    import torch
+    x = np.concatenate([np.linspace(0, 448, 20001, dtype=np.float32),
+                        (2.0 ** np.linspace(-12, 8.8, 10001)).astype(np.float32)])
+    bits, val = O.e4m3_round(x)
+    t = torch.from_numpy(x).to(torch.float8_e4m3fn)
+    assert np.array_equal(bits, t.view(torch.uint8).numpy())
+    assert np.array_equal(val, t.float().numpy())
+    assert np.array_equal(O.e4m3_bits_to_f32(bits), val)
+
+
+def test_nvfp4_gemm_oracle_is_dequant_matmul():
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal((3, 128)).astype(np.float32)
+    b = rng.standard_normal((5, 128)).astype(np.float32)
+    ap, asf, _ = O.nvfp4_quant(a, 2.0)
+    bp, bsf, _ = O.nvfp4_quant(b, 3.0)
+    out = O.nvfp4_gemm(ap, asf, bp, bsf, 1.0 / 6.0)
+    ref = (O.nvfp4_dequant(ap, asf) @ O.nvfp4_dequant(bp, bsf).T) * np.float64(np.float32(1.0 / 6.0))
+    assert np.array_equal(out, ref)
+    # dequantized values approximate x * gs (fp4 relative error < 1/3 per element, scale rounding aside)
+    assert np.abs(O.nvfp4_dequant(ap, asf) - a * 2.0).max() <= 0.5 * np.abs(a * 2.0).max()
