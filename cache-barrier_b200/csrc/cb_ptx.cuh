@@ -245,8 +245,10 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
 // this thread has completed.
 // Block-scaled FP4 MMA (NVFP4): A and B are e2m1 values packed two per byte,
 // K = 64 per instruction, one ue4m3 scale per 16 elements along K read from
-// tensor memory at sfa / sfb (the 4-column group a 32x128b.warpx4 copy of one
-// 512-byte scale atom fills), fp32 accumulator in d_tmem.
+// tensor memory in the layout a 32x128b.warpx4 copy of one 512-byte scale
+// atom gives: every lane quarter holds the atom's 32 rows of 16 bytes, lane
+// 32q + r columns sfa .. sfa + 3 = bytes 0..15 of atom row r. fp32 accumulator
+// in d_tmem.
 __device__ __forceinline__ void mma_nvf4_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                             uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
   asm volatile(
@@ -262,24 +264,6 @@ __device__ __forceinline__ void mma_nvf4_ss(uint32_t d_tmem, uint64_t a_desc, ui
 // K-major, ue4m3 scales (scale format 0), scale-factor ids 0, dense K = 64.
 __host__ __device__ constexpr uint32_t idesc_nvf4(int M, int N) {
   return (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
-}
-
-// Copies one 512-byte scale atom (32 rows of 16 bytes in shared memory) into
-// tensor memory at column `taddr`: each of the four 32-lane quarters receives
-// the 32 rows (lane l of a quarter gets row l % 32), 4 columns of 32 bits.
-__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t src_desc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc) : "memory");
-}
-
-// Shared-memory descriptor of a 512-byte scale atom for tcgen05.cp: K-major,
-// no swizzle, core matrices of 8 rows x 16 bytes stacked 128 bytes apart.
-__device__ __forceinline__ uint64_t smem_desc_sf_atom(uint32_t smem_addr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>(1u) << 16;                // leading byte offset (16 B; one 16-byte column)
-  d |= static_cast<uint64_t>(128u >> 4) << 32;          // stride byte offset: 128 B between 8-row groups
-  d |= static_cast<uint64_t>(1u) << 46;                 // descriptor version (sm_100)
-  return d;                                             // layout type 0: no swizzle
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -322,6 +306,12 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
       "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+}
+
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint4& v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
 }
 
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }

@@ -127,8 +127,9 @@ __global__ void __launch_bounds__(kQThreads) nvfp4_quant_kernel(const uint16_t* 
 constexpr int kBlockN = 128;       // weight rows per tile (MMA M)
 constexpr int kStageK = 256;       // k per stage: 128 packed bytes per row (one 128-byte swizzle row)
 constexpr int kStageRowBytes = 128;
-constexpr int kThreads = 224;
+constexpr int kThreads = 352;
 constexpr int kWaiterWarp = 6;
+constexpr int kSfWarp0 = 7;  // warps 7..10 write the block scales into tensor memory
 constexpr int kHandoffBar = 2;
 constexpr uint32_t kWTileBytes = kBlockN * kStageRowBytes;  // 16 KiB
 constexpr uint32_t kSfAtom = 512;
@@ -183,14 +184,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const Params p) {
   constexpr uint32_t kXTileBytes = TN * kStageRowBytes;
   constexpr uint32_t kAccCols = TN < 32 ? 32 : TN;
-  constexpr uint32_t kTmemCols = kAccCols + 32 <= 64 ? 64 : (kAccCols + 32 <= 128 ? 128 : 256);
-  constexpr uint32_t kSfaCol = kAccCols;       // 16 columns: 4 atoms x 4
-  constexpr uint32_t kSfbCol = kAccCols + 16;  // 16 columns
+  // two scale buffers of 32 columns (16 weight + 16 activation: 4 MMAs x 4)
+  constexpr uint32_t kTmemCols = kAccCols + 64 <= 128 ? 128 : 256;
+  constexpr uint32_t kSfCol0 = kAccCols;
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
   __shared__ __align__(8) uint64_t tfull_bar, tempty_bar, drain_bar;
+  __shared__ __align__(8) uint64_t sf_full[2];  // scale buffer b written for its k-block
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ int sh_issued, sh_consumed, sh_is_last;
@@ -218,6 +220,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&tfull_bar, 1);
     mbar_init(&tempty_bar, 4);
     mbar_init(&drain_bar, 1);
+    mbar_init(&sf_full[0], 4);
+    mbar_init(&sf_full[1], 4);
     abort_flag = 0;
     sh_issued = 0;
     sh_consumed = 0;
@@ -300,9 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    // Per stage: the scale atoms go to tensor memory (tcgen05.cp; executed in
-    // order with the MMAs this thread issues, so one scale buffer serves every
-    // stage), then one K = 64 MMA per atom.
+    // One K = 64 MMA per scale atom of the stage; the scales are already in
+    // tensor memory (buffer = local k-block parity, written by warps 7..10).
     const uint32_t idesc = idesc_nvf4(kBlockN, TN);
     int stage = 0;
     uint32_t acc_phase = 0;
@@ -331,15 +334,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int atoms = min(4, p.k_atoms - 4 * cur.kb);
           const uint32_t wa = smem_u32(smem_w + stage * kWTileBytes);
           const uint32_t xa = smem_u32(smem_x + stage * kXTileBytes);
-          const uint32_t sfw = smem_u32(smem_sfw + stage * kSfStage);
-          const uint32_t sfx = smem_u32(smem_sfx + stage * kSfStage);
+          const uint32_t sfa = tmem_d + kSfCol0 + 32 * (consumed & 1);
           for (int i = 0; i < atoms; ++i) {
-            tmem_cp_32x128b_warpx4(tmem_d + kSfaCol + 4 * i, smem_desc_sf_atom(sfw + i * kSfAtom));
-            tmem_cp_32x128b_warpx4(tmem_d + kSfbCol + 4 * i, smem_desc_sf_atom(sfx + i * kSfAtom));
-          }
-          for (int i = 0; i < atoms; ++i) {
-            mma_nvf4_ss(tmem_d, smem_desc_sw128(wa + i * 32), smem_desc_sw128(xa + i * 32), idesc,
-                        tmem_d + kSfaCol + 4 * i, tmem_d + kSfbCol + 4 * i, (first && i == 0) ? 0u : 1u);
+            mma_nvf4_ss(tmem_d, smem_desc_sw128(wa + i * 32), smem_desc_sw128(xa + i * 32), idesc, sfa + 4 * i,
+                        sfa + 16 + 4 * i, (first && i == 0) ? 0u : 1u);
           }
           mma_commit(&empty_bar[stage]);
         }
@@ -369,11 +367,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == kWaiterWarp) {
     // ---------------- stage waiter ----------------
+    // Hands k-block i to the MMA warp once its operands and its scales (buffer
+    // i & 1, phase (i >> 1) & 1) are in.
     int stage = 0;
     uint32_t phase = 0;
     for (long long g = g0; g < g1; ++g) {
+      const long long i = g - g0;
       bool bad = false;
-      if (lane == 0) bad = !mbar_wait(&full_bar[stage], phase, abort_ptr, p.status);
+      if (lane == 0) {
+        bad = !mbar_wait(&full_bar[stage], phase, abort_ptr, p.status);
+        if (!bad) bad = !mbar_wait(&sf_full[i & 1], static_cast<uint32_t>((i >> 1) & 1), abort_ptr, p.status);
+      }
       bad = __shfl_sync(0xffffffffu, bad, 0);
       if (named_bar_or(kHandoffBar, 64, bad)) break;
       if (++stage == S) {
@@ -382,6 +386,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
+  } else if (warp >= kSfWarp0) {
+    // ---------------- scale writers (warps 7..10) ----------------
+    // The scales go to tensor memory in the layout of a 32x128b.warpx4 copy of
+    // each 512-byte atom: warp w (lane quarter w % 4) writes, in every one of
+    // its 32 lanes r, the atom's row r (16 bytes = rows r, r+32, r+64, r+96 of
+    // the tile, four scales each) into 4 columns: buffer + 4 a for the weights'
+    // atom a, buffer + 16 + 4 a for the activations'. Buffer b = local k-block
+    // parity is rewritten for k-block i only after the MMAs of k-block i - 2
+    // completed (the commit that released their stage).
+    const int q = warp & 3;
+    const uint32_t rowoff = static_cast<uint32_t>(16 * lane);
+    int stage = 0;
+    uint32_t phase = 0;
+    KCursor cur;
+    cur.seek(p, g0);
+    for (long long g = g0; g < g1; ++g) {
+      const long long i = g - g0;
+      bool bad = false;
+      if (lane == 0) {
+        bad = !mbar_wait(&full_bar[stage], phase, abort_ptr, p.status);
+        if (!bad && i >= 2) {
+          const long long j = i - 2;
+          bad = !mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), abort_ptr, p.status);
+        }
+      }
+      if (__shfl_sync(0xffffffffu, bad, 0)) break;
+      const int atoms = min(4, p.k_atoms - 4 * cur.kb);
+      const uint8_t* sw = smem_sfw + stage * kSfStage + rowoff;
+      const uint8_t* sx = smem_sfx + stage * kSfStage + rowoff;
+      const uint32_t col = tmem_d + (static_cast<uint32_t>(q * 32) << 16) + kSfCol0 + 32 * (i & 1);
+      tc_fence_after();
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        if (a < atoms) {
+          tmem_st4(col + 4 * a, *reinterpret_cast<const uint4*>(sw + a * kSfAtom));
+          tmem_st4(col + 16 + 4 * a, *reinterpret_cast<const uint4*>(sx + a * kSfAtom));
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sf_full[i & 1]);
+      cur.next(p);
+      if (++stage == S) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     pdl_wait_primary();
