@@ -184,15 +184,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const Params p) {
   constexpr uint32_t kXTileBytes = TN * kStageRowBytes;
   constexpr uint32_t kAccCols = TN < 32 ? 32 : TN;
-  // two scale buffers of 32 columns (16 weight + 16 activation: 4 MMAs x 4)
-  constexpr uint32_t kTmemCols = kAccCols + 64 <= 128 ? 128 : 256;
+  // one scale buffer of 32 columns per ring stage (16 weight + 16 activation:
+  // 4 MMAs x 4), after the accumulator; the launcher keeps kAccCols + 32 S <= 512
+  constexpr uint32_t kTmemCols = 512;
   constexpr uint32_t kSfCol0 = kAccCols;
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_bar[kMaxStages];
+  __shared__ __align__(8) uint64_t full_bar[kMaxStages];   // weight + activation tiles landed
+  __shared__ __align__(8) uint64_t sfdat_bar[kMaxStages];  // the stage's scale atoms landed
   __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
   __shared__ __align__(8) uint64_t tfull_bar, tempty_bar, drain_bar;
-  __shared__ __align__(8) uint64_t sf_full[2];  // scale buffer b written for its k-block
+  __shared__ __align__(8) uint64_t sf_full[kMaxStages];  // the stage's scales are in tensor memory
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ int sh_issued, sh_consumed, sh_is_last;
@@ -215,13 +217,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_launch_dependents();
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
+      mbar_init(&sfdat_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(&tfull_bar, 1);
     mbar_init(&tempty_bar, 4);
     mbar_init(&drain_bar, 1);
-    mbar_init(&sf_full[0], 4);
-    mbar_init(&sf_full[1], 4);
+    for (int b = 0; b < S; ++b) mbar_init(&sf_full[b], 4);
     abort_flag = 0;
     sh_issued = 0;
     sh_consumed = 0;
@@ -249,16 +251,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t pol_x = policy_evict_last();
     const long long nmine = g1 - g0;
     const int pro = static_cast<int>(nmine < S ? nmine : S);
+    // Scale atoms go out ahead of their stage's tiles (their own barrier), so
+    // the scale writers can place them in tensor memory before the tiles land.
     if (lane < pro) {
       KCursor c;
       c.seek(p, g0 + lane);
       const int atoms = min(4, p.k_atoms - 4 * c.kb);
-      mbar_arrive_expect_tx(&full_bar[lane], kWTileBytes + kXTileBytes + 2u * atoms * kSfAtom);
-      tma_load_3d(smem_w + lane * kWTileBytes, &tmap_w, &full_bar[lane], c.kb * kStageRowBytes, c.nt * kBlockN, 0,
-                  pol_w);
+      mbar_arrive_expect_tx(&sfdat_bar[lane], 2u * atoms * kSfAtom);
       bulk_copy_g2s(smem_sfw + lane * kSfStage,
                     p.sfw + (static_cast<long long>(c.nt) * p.k_atoms + 4 * c.kb) * kSfAtom, atoms * kSfAtom,
-                    &full_bar[lane], pol_w);
+                    &sfdat_bar[lane], pol_w);
+      mbar_arrive_expect_tx(&full_bar[lane], kWTileBytes + kXTileBytes);
+      tma_load_3d(smem_w + lane * kWTileBytes, &tmap_w, &full_bar[lane], c.kb * kStageRowBytes, c.nt * kBlockN, 0,
+                  pol_w);
     }
     __syncwarp();
     pdl_wait_primary();
@@ -266,10 +271,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       KCursor c;
       c.seek(p, g0 + lane);
       const int atoms = min(4, p.k_atoms - 4 * c.kb);
-      tma_load_3d(smem_x + lane * kXTileBytes, &tmap_x, &full_bar[lane], c.kb * kStageRowBytes, c.mt * TN, 0, pol_x);
       bulk_copy_g2s(smem_sfx + lane * kSfStage,
                     p.sfx + (static_cast<long long>((c.mt * TN) >> 7) * p.k_atoms + 4 * c.kb) * kSfAtom,
-                    atoms * kSfAtom, &full_bar[lane], pol_x);
+                    atoms * kSfAtom, &sfdat_bar[lane], pol_x);
+      tma_load_3d(smem_x + lane * kXTileBytes, &tmap_x, &full_bar[lane], c.kb * kStageRowBytes, c.mt * TN, 0, pol_x);
     }
     __syncwarp();
     if (lane == 0) {
@@ -281,17 +286,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (long long g = g0 + pro; g < g1; ++g) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_ptr, p.status)) break;
         const int atoms = min(4, p.k_atoms - 4 * cur.kb);
-        mbar_arrive_expect_tx(&full_bar[stage], kWTileBytes + kXTileBytes + 2u * atoms * kSfAtom);
-        tma_load_3d(smem_w + stage * kWTileBytes, &tmap_w, &full_bar[stage], cur.kb * kStageRowBytes,
-                    cur.nt * kBlockN, 0, pol_w);
+        mbar_arrive_expect_tx(&sfdat_bar[stage], 2u * atoms * kSfAtom);
         bulk_copy_g2s(smem_sfw + stage * kSfStage,
                       p.sfw + (static_cast<long long>(cur.nt) * p.k_atoms + 4 * cur.kb) * kSfAtom, atoms * kSfAtom,
-                      &full_bar[stage], pol_w);
-        tma_load_3d(smem_x + stage * kXTileBytes, &tmap_x, &full_bar[stage], cur.kb * kStageRowBytes, cur.mt * TN, 0,
-                    pol_x);
+                      &sfdat_bar[stage], pol_w);
         bulk_copy_g2s(smem_sfx + stage * kSfStage,
                       p.sfx + (static_cast<long long>((cur.mt * TN) >> 7) * p.k_atoms + 4 * cur.kb) * kSfAtom,
-                      atoms * kSfAtom, &full_bar[stage], pol_x);
+                      atoms * kSfAtom, &sfdat_bar[stage], pol_x);
+        mbar_arrive_expect_tx(&full_bar[stage], kWTileBytes + kXTileBytes);
+        tma_load_3d(smem_w + stage * kWTileBytes, &tmap_w, &full_bar[stage], cur.kb * kStageRowBytes,
+                    cur.nt * kBlockN, 0, pol_w);
+        tma_load_3d(smem_x + stage * kXTileBytes, &tmap_x, &full_bar[stage], cur.kb * kStageRowBytes, cur.mt * TN, 0,
+                    pol_x);
         cur.next(p);
         ++issued;
         if (++stage == S) {
@@ -305,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     // One K = 64 MMA per scale atom of the stage; the scales are already in
-    // tensor memory (buffer = local k-block parity, written by warps 7..10).
+    // tensor memory (the stage's buffer, written by warps 7..10).
     const uint32_t idesc = idesc_nvf4(kBlockN, TN);
     int stage = 0;
     uint32_t acc_phase = 0;
@@ -334,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int atoms = min(4, p.k_atoms - 4 * cur.kb);
           const uint32_t wa = smem_u32(smem_w + stage * kWTileBytes);
           const uint32_t xa = smem_u32(smem_x + stage * kXTileBytes);
-          const uint32_t sfa = tmem_d + kSfCol0 + 32 * (consumed & 1);
+          const uint32_t sfa = tmem_d + kSfCol0 + 32 * stage;
           for (int i = 0; i < atoms; ++i) {
             mma_nvf4_ss(tmem_d, smem_desc_sw128(wa + i * 32), smem_desc_sw128(xa + i * 32), idesc, sfa + 4 * i,
                         sfa + 16 + 4 * i, (first && i == 0) ? 0u : 1u);
@@ -367,16 +373,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == kWaiterWarp) {
     // ---------------- stage waiter ----------------
-    // Hands k-block i to the MMA warp once its operands and its scales (buffer
-    // i & 1, phase (i >> 1) & 1) are in.
+    // Hands a k-block to the MMA warp once its operands and its scales (the
+    // stage's buffer, same phase) are in.
     int stage = 0;
     uint32_t phase = 0;
     for (long long g = g0; g < g1; ++g) {
-      const long long i = g - g0;
       bool bad = false;
       if (lane == 0) {
         bad = !mbar_wait(&full_bar[stage], phase, abort_ptr, p.status);
-        if (!bad) bad = !mbar_wait(&sf_full[i & 1], static_cast<uint32_t>((i >> 1) & 1), abort_ptr, p.status);
+        if (!bad) bad = !mbar_wait(&sf_full[stage], phase, abort_ptr, p.status);
       }
       bad = __shfl_sync(0xffffffffu, bad, 0);
       if (named_bar_or(kHandoffBar, 64, bad)) break;
@@ -392,9 +397,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // each 512-byte atom: warp w (lane quarter w % 4) writes, in every one of
     // its 32 lanes r, the atom's row r (16 bytes = rows r, r+32, r+64, r+96 of
     // the tile, four scales each) into 4 columns: buffer + 4 a for the weights'
-    // atom a, buffer + 16 + 4 a for the activations'. Buffer b = local k-block
-    // parity is rewritten for k-block i only after the MMAs of k-block i - 2
-    // completed (the commit that released their stage).
+    // atom a, buffer + 16 + 4 a for the activations'. Each ring stage has its
+    // own buffer: the stage's scale atoms land only after the producer refilled
+    // the stage, i.e. after the MMAs that read the buffer's previous contents
+    // completed, so the writers wait for nothing but the atoms.
     const int q = warp & 3;
     const uint32_t rowoff = static_cast<uint32_t>(16 * lane);
     int stage = 0;
@@ -402,20 +408,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     KCursor cur;
     cur.seek(p, g0);
     for (long long g = g0; g < g1; ++g) {
-      const long long i = g - g0;
       bool bad = false;
-      if (lane == 0) {
-        bad = !mbar_wait(&full_bar[stage], phase, abort_ptr, p.status);
-        if (!bad && i >= 2) {
-          const long long j = i - 2;
-          bad = !mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), abort_ptr, p.status);
-        }
-      }
+      if (lane == 0) bad = !mbar_wait(&sfdat_bar[stage], phase, abort_ptr, p.status);
       if (__shfl_sync(0xffffffffu, bad, 0)) break;
       const int atoms = min(4, p.k_atoms - 4 * cur.kb);
       const uint8_t* sw = smem_sfw + stage * kSfStage + rowoff;
       const uint8_t* sx = smem_sfx + stage * kSfStage + rowoff;
-      const uint32_t col = tmem_d + (static_cast<uint32_t>(q * 32) << 16) + kSfCol0 + 32 * (i & 1);
+      const uint32_t col = tmem_d + (static_cast<uint32_t>(q * 32) << 16) + kSfCol0 + 32 * static_cast<uint32_t>(stage);
       tc_fence_after();
 #pragma unroll
       for (int a = 0; a < 4; ++a) {
@@ -427,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sf_full[i & 1]);
+      if (lane == 0) mbar_arrive(&sf_full[stage]);
       cur.next(p);
       if (++stage == S) {
         stage = 0;
@@ -515,7 +514,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 0) {
     if (lane == 0 && abort_flag) {
-      for (int j = sh_consumed; j < sh_issued; ++j) mbar_wait(&full_bar[j % S], (j / S) & 1, nullptr, p.status);
+      for (int j = sh_consumed; j < sh_issued; ++j) {
+        mbar_wait(&full_bar[j % S], (j / S) & 1, nullptr, p.status);
+        mbar_wait(&sfdat_bar[j % S], (j / S) & 1, nullptr, p.status);
+      }
     }
     __syncwarp();
   }
@@ -626,6 +628,9 @@ int launch_nvfp4_gemm(const Nvfp4Launch& L, cudaStream_t stream) {
   const size_t stage_bytes = kWTileBytes + static_cast<size_t>(TN) * kStageRowBytes + 2 * kSfStage;
   int stages = static_cast<int>((200u * 1024u) / stage_bytes);
   if (stages > kMaxStages) stages = kMaxStages;
+  // one 32-column scale buffer per stage after the accumulator, in 512 columns
+  const int acc_cols = TN < 32 ? 32 : TN;
+  if (stages > (512 - acc_cols) / 32) stages = (512 - acc_cols) / 32;
   if (stages < 2) stages = 2;
   p.stages = stages;
   p.sk.total = total;
