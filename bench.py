@@ -19,8 +19,8 @@ Reported (one JSON line from rank 0):
              pinned host activations copied in and outputs copied out every GEMM
   roofline   the GEMM kernel alone: algorithmic bytes per launch / CUDA-event time
   cpu_baseline  the oracle's restatement of the reference's CPU path (rank 0, N = 1)
-plus the cuBLAS bf16 comparison (dequantized weights, same rotation) and a W4A16
-group-128 measurement of the same shape.
+plus the cuBLAS bf16 comparison (dequantized weights, same rotation), and W4A16
+group-128 and NVFP4 (block-scaled FP4 tensor cores) measurements of the same shape.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 """
@@ -172,6 +172,11 @@ def committed_traffic(name):
 
 def w8a8_bytes(T):
     return K_DIM * N_DIM + 4 * N_DIM + T * K_DIM + 4 * T + 2 * T * N_DIM
+
+
+def nvfp4_bytes(T):
+    """Packed e2m1 weights and activations with their e4m3 scales (one per 16), bf16 out."""
+    return K_DIM * N_DIM // 2 + K_DIM * N_DIM // 16 + T * K_DIM // 2 + T * K_DIM // 16 + 2 * T * N_DIM
 
 
 def w4a16_bytes(T):
@@ -401,6 +406,53 @@ def main():
     except Exception as e:  # noqa: BLE001
         w4 = {"error": repr(e)}
 
+    # ---------------- NVFP4 W4A4 (e2m1 + e4m3 block scales), same shape ----------------
+    fp4 = None
+    try:
+        gen5 = torch.Generator(device=dev).manual_seed(77 + rank)
+        fp4_w = []
+        for _ in range(COPIES):
+            wb = (torch.randn(N_DIM, K_DIM, generator=gen5, device=dev) / K_DIM ** 0.5).to(torch.bfloat16)
+            gw = torch.tensor([448.0 * 6.0 / float(wb.float().abs().max())], device=dev)
+            fq, fsf = ops.nvfp4_quantize(wb, gw)
+            fp4_w.append((fq, fsf, gw))
+            del wb
+        fo = {T: torch.empty(T, N_DIM, dtype=torch.bfloat16, device=dev) for T in TOKENS}
+        fp4_t, fp4_dyn_t = {}, {}
+        for T in TOKENS:
+            gx = torch.tensor([448.0 * 6.0 / float(acts[T].float().abs().max())], device=dev)
+            qx, sx = ops.nvfp4_quantize(acts[T], gx)
+            alphas = [(1.0 / (gx * gw)).float() for (_, _, gw) in fp4_w]
+
+            def f(T=T, qx=qx, sx=sx, alphas=alphas):
+                for c in range(CYCLES):
+                    ops.nvfp4_gemm(qx, sx, fp4_w[c % COPIES][0], fp4_w[c % COPIES][1], alphas[c % COPIES],
+                                   out=fo[T])
+
+            def fd(T=T, qx=qx, sx=sx, alphas=alphas, gx=gx):
+                for c in range(CYCLES):
+                    ops.nvfp4_quantize(acts[T], gx, q=qx, sf=sx)
+                    ops.nvfp4_gemm(qx, sx, fp4_w[c % COPIES][0], fp4_w[c % COPIES][1], alphas[c % COPIES],
+                                   out=fo[T])
+            for fn, dst in ((f, fp4_t), (fd, fp4_dyn_t)):
+                g = capture(fn)
+                dst[T] = time_replays(g, 10, 2) * 1e3 / CYCLES
+                del g
+        fmean = statistics.mean(fp4_t.values())
+        fdyn = statistics.mean(fp4_dyn_t.values())
+        fbytes = statistics.mean(nvfp4_bytes(T) for T in TOKENS)
+        fp4 = {"us_per_gemm": round(fmean, 3), "per_token_us": {str(T): round(v, 3) for T, v in fp4_t.items()},
+               "us_per_gemm_with_act_quant": round(fdyn, 3),
+               "achieved_gbs": round(fbytes / (fmean * 1e-6) / 1e9, 1),
+               "frac_of_measured_hbm": round(fbytes / (fmean * 1e-6) / 1e9 / peaks["hbm_gbs"], 3),
+               "speedup_vs_cublas_bf16": round(cub_mean / fmean, 3),
+               "speedup_vs_cublas_bf16_with_act_quant": round(cub_mean / fdyn, 3),
+               "config": f"K=N=8192 NVFP4 (vLLM formats: e2m1 + e4m3 scales per 16, amax global scales), "
+                         f"{COPIES} rotating copies (144 MiB > L2), bf16 acts/out"}
+        assert ops.device_status(dev) == 0
+    except Exception as e:  # noqa: BLE001
+        fp4 = {"error": repr(e)}
+
     # ---------------- CPU baseline (rank 0, N = 1) ----------------
     cpu = None
     if world == 1 and rank == 0:
@@ -457,9 +509,10 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_us, 3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "w8a8_bmm.w8a8_bmm_full (eager, pinned host in/out per GEMM)"},
-            "gpu_launches": args.steps * gemms_per_step * 2,
+            "gpu_launches": args.steps * gemms_per_step * 2,  # timed region: act-quant + GEMM per GEMM
             "clocks": clock_info,
             "w4a16": w4,
+            "nvfp4": fp4,
         }
         print(json.dumps(line), flush=True)
 
