@@ -28,7 +28,7 @@ from cb200 import ops  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["w8a8", "w8a8_dynamic", "w4a16"], default="w8a8")
+    ap.add_argument("--op", choices=["w8a8", "w8a8_dynamic", "w4a16", "nvfp4"], default="w8a8")
     ap.add_argument("--tokens", type=int, default=32)
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192)
@@ -53,6 +53,20 @@ def main():
                 ops.w8a8_gemm(q, weights[i % args.copies], s, ws_, out=out)
             else:
                 ops.w8a8_gemm_dynamic(a, weights[i % args.copies], ws_, q=q, s=s, out=out)
+    elif args.op == "nvfp4":
+        gx = torch.tensor([448.0 * 6.0 / float(a.float().abs().max())], device=dev)
+        qa, sa = ops.nvfp4_quantize(a, gx)
+        weights = []
+        for _ in range(args.copies):
+            w = (torch.randn(N, K, generator=g, device=dev) / K ** 0.5).to(torch.bfloat16)
+            gw = torch.tensor([448.0 * 6.0 / float(w.float().abs().max())], device=dev)
+            qw, sw = ops.nvfp4_quantize(w, gw)
+            weights.append((qw, sw, (1.0 / (gx * gw)).float()))
+            del w
+
+        def run(i):
+            qw, sw, alpha = weights[i % args.copies]
+            ops.nvfp4_gemm(qa, sa, qw, sw, alpha, out=out)
     else:
         sc = ((torch.randn(K // 128, N, generator=g, device=dev) * 0.02).abs() / 7 + 1e-4).to(torch.bfloat16)
         weights = [ops.repack_w4(torch.randint(0, 256, (K // 2, N), generator=g, dtype=torch.uint8, device=dev),
