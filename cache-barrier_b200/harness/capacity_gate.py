@@ -8,7 +8,11 @@ kernels. Two shape families:
                     effective L2 capacity C_eff; W4A16 with g128 scales
                     (dense_ops.quantize_w4a16 / apply_w4a16_linear), W8A8 with
                     dynamic per-token act quant inside the timed region
-                    (ops.w8a8_gemm_dynamic), bf16 cuBLAS torch.mm.
+                    (ops.w8a8_gemm_dynamic), NVFP4 W4A4 on the block-scaled
+                    FP4 tensor cores with the activations quantized per call
+                    (ops.nvfp4_quantize + ops.nvfp4_gemm; the reference's
+                    matched-precision path, profiling/cuda_validation/
+                    bench_moe_nvfp4_native.py), bf16 cuBLAS torch.mm.
   bmm               the reference's batched family H = 128, K = 128,
                     N = 32 * W_MB (bench_capacity_gate.py:80-83), driven
                     through the drop-in names exactly as the reference harness
@@ -98,7 +102,30 @@ def square_cell(K: int, T: int, c_eff_mb: float, flushed: bool, reps: int) -> di
         lambda i: (lambda: dense_ops.apply_w4a16_linear(x, w4[i % R4][0], w4[i % R4][1], N, K, out=out)),
         reps=reps)
     r["w4a16_copies"] = R4
-    del w4, wb
+    del w4
+
+    # NVFP4 (e2m1 + e4m3 scales per 16; amax global scales as the reference's harness)
+    RF = copies_for(K * N // 2 + K * N // 16, c_eff_mb, flushed)
+    gx = torch.tensor([448.0 * 6.0 / float(x.float().abs().max())], device=dev)
+    qx, sx = ops.nvfp4_quantize(x, gx)
+    wf4 = []
+    for i in range(RF):
+        gw = torch.tensor([448.0 * 6.0 / float(wb[i % R].float().abs().max())], device=dev)
+        qw, sw = ops.nvfp4_quantize(wb[i % R], gw)
+        wf4.append((qw, sw, (1.0 / (gx * gw)).float()))
+
+    def fp4_dyn(i):
+        def f():
+            ops.nvfp4_quantize(x, gx, q=qx, sf=sx)
+            ops.nvfp4_gemm(qx, sx, wf4[i % RF][0], wf4[i % RF][1], wf4[i % RF][2], out=out)
+        return f
+
+    r["nvfp4_us"] = graph_time_us_indexed(fp4_dyn, reps=reps)
+    r["nvfp4_mm_us"] = graph_time_us_indexed(
+        lambda i: (lambda: ops.nvfp4_gemm(qx, sx, wf4[i % RF][0], wf4[i % RF][1], wf4[i % RF][2], out=out)),
+        reps=reps)
+    r["nvfp4_copies"] = RF
+    del wf4, wb
     torch.cuda.empty_cache()
     return r
 
@@ -207,11 +234,16 @@ def main():
                     r.update({"tokens": T, "variant": variant})
                     r["sp_w8a8"] = round(r["bf16_us"] / r["w8a8_us"], 4)
                     r["sp_w4a16"] = round(r["bf16_us"] / r["w4a16_us"], 4)
+                    if "nvfp4_us" in r:
+                        r["sp_nvfp4"] = round(r["bf16_us"] / r["nvfp4_us"], 4)
                     rows.append(r)
                     print(f"{variant:7s} T={T:4d} W={r['w_mb']:8.1f} MB  bf16 {r['bf16_us']:8.2f}  "
                           f"w8a8 {r['w8a8_us']:8.2f} ({r['sp_w8a8']:.2f}x)  "
-                          f"w4a16 {r['w4a16_us']:8.2f} ({r['sp_w4a16']:.2f}x)", flush=True)
-    gates = {v: {str(T): {p: gate_of(rows, p, T, v) for p in ("w8a8", "w4a16")} for T in tsweep}
+                          f"w4a16 {r['w4a16_us']:8.2f} ({r['sp_w4a16']:.2f}x)"
+                          + (f"  nvfp4 {r['nvfp4_us']:8.2f} ({r['sp_nvfp4']:.2f}x)" if "nvfp4_us" in r else ""),
+                          flush=True)
+    precs = ("w8a8", "w4a16", "nvfp4") if args.family == "square" else ("w8a8", "w4a16")
+    gates = {v: {str(T): {p: gate_of(rows, p, T, v) for p in precs} for T in tsweep}
              for v in args.variants.split(",")}
     out = {"experiment": f"capacity_gate_{args.family}", "gpu": gpu_info(), "c_eff_mb": c_eff,
            "timing": "CUDA graphs, 10 launches/graph, median of replays; flushed = rotating weight copies",
