@@ -241,8 +241,6 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       : "memory");
 }
 
-// Arrives once on the mbarrier when every previously issued tcgen05 async op of
-// this thread has completed.
 // Block-scaled FP4 MMA (NVFP4): A and B are e2m1 values packed two per byte,
 // K = 64 per instruction, one ue4m3 scale per 16 elements along K read from
 // tensor memory in the layout a 32x128b.warpx4 copy of one 512-byte scale
@@ -266,6 +264,8 @@ __host__ __device__ constexpr uint32_t idesc_nvf4(int M, int N) {
   return (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Arrives once on the mbarrier when every previously issued tcgen05 async op of
+// this thread has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))

@@ -11,16 +11,21 @@
 // Work: the (panel, m-tile) pairs, a panel being the weights of one batch
 // entry and 128 output columns (its K / 128 native 8 KiB tiles), split into
 // contiguous ranges over the SMs. For each run of m-tiles of one panel a CTA
-//   1. copies the packed panel with one cp.async.bulk (warp 0) and dequantizes
-//      it once into shared memory as the MMA's B operand (N = 128 columns x K,
-//      K-major, 128-byte swizzle; g128 scales folded in) (warps 2-5);
-//   2. streams the activation m-tiles through a TMA ring of 128-row x 64-k boxes
-//      (warp 0); warp 6 waits for each box and hands it to warp 1 over a named
-//      barrier; warp 1 issues tcgen05.mma kind::f16 with A = activations
-//      (M = 128 rows), B = the resident panel (N = 128), fp32 accumulators in
-//      TMEM, double-buffered across m-tiles;
+//   1. dequantizes the panel once into tensor memory as the MMA's A operand
+//      (M = 128 output columns in the lanes, K along the columns as bf16/f16
+//      pairs; g128 scales folded in): warps 2-5 read the packed tiles from
+//      global memory and write them with tcgen05.st (warp w owns lanes
+//      32 (w % 4) .. +31);
+//   2. streams the activation m-tiles through a TMA ring of 128-token x 64-k
+//      boxes that has all of shared memory (warp 0); warp 6 waits for each box
+//      and hands it to warp 1 over a named barrier; warp 1 issues tcgen05.mma
+//      kind::f16 with A = the panel in tensor memory, B = the token box
+//      (N = 128 tokens), fp32 accumulators [128 columns x 128 tokens] in TMEM,
+//      double-buffered across m-tiles;
 //   3. warps 2-5 convert each finished accumulator (per-channel scale applied
-//      in fp32 here when G >= K) and store it while the MMA fills the other.
+//      in fp32 here when G >= K): the thread of lane n stores output column n
+//      for the tile's 128 tokens, so each store of a warp covers 32 adjacent
+//      columns of one token row.
 // Runs that start a new panel wait until the previous panel's MMAs are done
 // (its last accumulator was drained) before overwriting it.
 #include <cuda.h>
@@ -37,8 +42,8 @@
 namespace cb {
 namespace {
 
-constexpr int kBM = 128;               // token rows per m-tile (MMA M)
-constexpr int kBN = 128;               // output columns per panel (MMA N)
+constexpr int kBM = 128;               // tokens per m-tile (MMA N)
+constexpr int kBN = 128;               // output columns per panel (MMA M)
 constexpr int kBK = 128;               // k per weight tile
 constexpr int kMaxKB = 4;              // resident panels up to K = 512
 constexpr int kThreads = 7 * 32;       // producer, MMA, 4 dequant/epilogue warps, stage waiter
@@ -46,10 +51,10 @@ constexpr int kWaiterWarp = 6;
 constexpr int kPanelBar = 2;           // named barrier: epilogue warps (arrive) -> MMA warp (sync)
 constexpr int kPanelCount = 5 * 32;
 constexpr int kStageBar = 3;           // named barrier: stage waiter <-> MMA warp
-constexpr uint32_t kBoxBytes = kBM * 128;         // 128 rows x 64 16-bit k
-constexpr uint32_t kPanelTileBytes = kBN * kBK * 2;  // one dequantized k-block of the panel
+constexpr uint32_t kBoxBytes = kBM * 128;         // 128 tokens x 64 16-bit k
 constexpr uint32_t kPackedTileBytes = kBN * kBK / 2;
-constexpr uint32_t kTmemCols = 2 * kBN;           // two accumulators of 128 fp32 columns
+constexpr uint32_t kPanelCol = 2 * kBM;           // after two accumulators of 128 fp32 columns
+constexpr uint32_t kTmemCols = 512;               // + the panel: 64 columns per 128 k, K <= 512
 constexpr int kMaxRingStages = 16;
 
 struct RParams {
@@ -66,41 +71,11 @@ struct RParams {
   void* out;
   int out_dtype;
   long long out_sb, out_sm;
-  int vec_store;              // 16-byte output stores allowed
   int* status;
 };
 
 __device__ __forceinline__ long long range_start(const RParams& p, int c) {
   return static_cast<long long>(c) * p.items / gridDim.x;
-}
-
-template <int OUT>
-__device__ __forceinline__ void store16(const RParams& p, long long base, const float (&v)[16], int ncols) {
-  // OUT: 0 = f16, 1 = bf16, 2 = f32 (the output dtype's code)
-  if (p.vec_store && ncols == 16) {
-    if constexpr (OUT == CB_DTYPE_F32) {
-      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + base);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-    } else {
-      uint32_t w[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if constexpr (OUT == CB_DTYPE_BF16) {
-          __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
-          w[q] = *reinterpret_cast<uint32_t*>(&h);
-        } else {
-          __half2 h = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
-          w[q] = *reinterpret_cast<uint32_t*>(&h);
-        }
-      }
-      uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + base);
-      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    }
-  } else {
-    for (int j = 0; j < ncols; ++j) store_elem(p.out, OUT, base + j, v[j]);
-  }
 }
 
 template <typename T, int OUT>
@@ -109,18 +84,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kMaxRingStages];
   __shared__ __align__(8) uint64_t empty_bar[kMaxRingStages];
-  __shared__ __align__(8) uint64_t packed_full, packed_empty, drain_bar;
+  __shared__ __align__(8) uint64_t drain_bar;
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2];
-  __shared__ float col_scale[kBN];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
-  __shared__ int sh_issued, sh_consumed, sh_packed_issued, sh_packed_used;
+  __shared__ int sh_issued, sh_consumed;
   volatile int* abort_ptr = &abort_flag;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* panel = smem;                                      // kb x 32 KiB, dequantized B operand
-  uint8_t* packed = panel + p.kb * kPanelTileBytes;           // kb x 8 KiB native tiles
-  uint8_t* ring = packed + p.kb * kPackedTileBytes;           // stages x 16 KiB activation boxes
+  uint8_t* ring = smem;  // stages x 16 KiB activation boxes
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -135,15 +107,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&packed_full, 1);
-    mbar_init(&packed_empty, 4);
     mbar_init(&drain_bar, 1);
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 4);
     }
     abort_flag = 0;
-    sh_issued = sh_consumed = sh_packed_issued = sh_packed_used = 0;
+    sh_issued = sh_consumed = 0;
     fence_mbar_init();
     prefetch_tmap(&tmap_a);
   }
@@ -161,22 +131,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- producer ----------------
-      const uint64_t pol_w = policy_evict_last();   // panels are small and shared by the CTAs of a panel
       // activations stream once, or twice at about the same time when the CTAs of two
       // column panels of one batch entry walk the same m-tiles: keep them normal
       const uint64_t pol_a = policy_evict_normal();
       int stage = 0;
       uint32_t phase = 0;
-      int issued = 0, runs = 0;
+      int issued = 0;
       bool ok = true;
+      pdl_wait_primary();  // activations come from the preceding kernel
       for (long long i = i0; i < i1 && ok;) {
         const long long pan = i / p.m_tiles;
         const long long run_end = (pan + 1) * p.m_tiles < i1 ? (pan + 1) * p.m_tiles : i1;
-        if (runs > 0 && !mbar_wait(&packed_empty, static_cast<uint32_t>((runs - 1) & 1), abort_ptr, p.status)) break;
-        mbar_arrive_expect_tx(&packed_full, p.kb * kPackedTileBytes);
-        bulk_copy_g2s(packed, p.w + pan * p.kb * kPackedTileBytes, p.kb * kPackedTileBytes, &packed_full, pol_w);
-        ++runs;
-        if (runs == 1) pdl_wait_primary();  // activations come from the preceding kernel
         const int h = static_cast<int>(pan / p.n_tiles);
         for (; i < run_end && ok; ++i) {
           const int mt = static_cast<int>(i % p.m_tiles);
@@ -196,23 +161,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       sh_issued = issued;
-      sh_packed_issued = runs;
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    const uint32_t idesc = idesc_f16_f32(kBM, kBN, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
+    const uint32_t idesc = idesc_f16_f32(kBN, kBM, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
     int stage = 0, consumed = 0, tiles = 0;
     bool bad = false, stop = false;
     for (long long i = i0; i < i1 && !stop;) {
       const long long pan = i / p.m_tiles;
       const long long run_end = (pan + 1) * p.m_tiles < i1 ? (pan + 1) * p.m_tiles : i1;
-      named_bar_sync(kPanelBar, kPanelCount);  // the panel for this run is dequantized
+      named_bar_sync(kPanelBar, kPanelCount);  // the panel for this run is in tensor memory
       for (; i < run_end && !stop; ++i) {
         const int acc = tiles & 1;
         if (lane == 0 && !bad && tiles >= 2)
           bad = !mbar_wait(&acc_empty[acc], static_cast<uint32_t>(((tiles >> 1) - 1) & 1), abort_ptr, p.status);
-        const uint32_t d = tmem_base + acc * kBN;
+        const uint32_t d = tmem_base + acc * kBM;
         for (int bx = 0; bx < boxes_per_tile; ++bx) {
           if (named_bar_or(kStageBar, 64, bad)) {
             stop = true;
@@ -220,12 +184,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (lane == 0) {
             tc_fence_after();
-            const uint32_t a0 = smem_u32(ring + stage * kBoxBytes);
-            const uint32_t b0 = smem_u32(panel + (bx >> 1) * kPanelTileBytes + (bx & 1) * (kPanelTileBytes / 2));
+            // box bx = k 64 bx .. 64 bx + 63: panel columns 32 bx .. (two k per column)
+            const uint32_t b0 = smem_u32(ring + stage * kBoxBytes);
+            const uint32_t a0 = tmem_base + kPanelCol + 32 * bx;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              mma_f16_ss(d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
-                         (bx == 0 && kk == 0) ? 0u : 1u);
+              mma_f16_ts(d, a0 + kk * 8, smem_desc_sw128(b0 + kk * 32), idesc, (bx == 0 && kk == 0) ? 0u : 1u);
             mma_commit(&empty_bar[stage]);
           }
           __syncwarp();
@@ -276,63 +240,63 @@ __global__ void __launch_bounds__(kThreads, 1)
     // arrival still happens.
     pdl_wait_primary();  // the output may still be read by the preceding kernel
     const int quarter = warp & 3;
-    const int erow = quarter * 32 + lane;  // TMEM lane = token row within the m-tile
-    const int drow = threadIdx.x - 64;     // panel row (output column) this thread dequantizes
+    const int row = quarter * 32 + lane;  // TMEM lane = panel row = output column within the panel
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    int runs = 0, tiles = 0;
+    int tiles = 0;
     for (long long i = i0; i < i1;) {
       const long long pan = i / p.m_tiles;
       const long long run_end = (pan + 1) * p.m_tiles < i1 ? (pan + 1) * p.m_tiles : i1;
       const int h = static_cast<int>(pan / p.n_tiles);
       const int nt = static_cast<int>(pan % p.n_tiles);
-      const int n_dq = nt * kBN + drow;
-      // 1. dequantize the panel (the previous run's MMAs are done: its last
-      //    accumulator was drained below before this point)
-      const bool got = mbar_wait(&packed_full, static_cast<uint32_t>(runs & 1), abort_ptr, p.status);
-      if (__all_sync(0xffffffffu, got)) {
-        if (p.per_channel)
-          col_scale[drow] = n_dq < p.N ? load_elem(p.scales, p.scale_dtype, h * p.s_sb + n_dq) : 0.0f;
-        for (int kb = 0; kb < p.kb; ++kb) {
-          float sv = 1.0f;
-          if (!p.per_channel && n_dq < p.N)
-            sv = load_elem(p.scales, p.scale_dtype, h * p.s_sb + (kb / p.kb_per_group) * p.s_sg + n_dq);
-          uint32_t r[64];
-          dequant_native_row<T>(packed + kb * kPackedTileBytes, drow, Dq<T>::from_f(sv), !p.per_channel, r);
-          store_row_sw128(panel + kb * kPanelTileBytes, drow, r);
+      const int n = nt * kBN + row;
+      // 1. dequantize the panel into tensor memory (the previous run's MMAs
+      //    are done: its last accumulator was drained below before this point)
+      float col_scale = 1.0f;
+      if (p.per_channel && n < p.N) col_scale = load_elem(p.scales, p.scale_dtype, h * p.s_sb + n);
+      for (int kb = 0; kb < p.kb; ++kb) {
+        float sv = 1.0f;
+        if (!p.per_channel && n < p.N)
+          sv = load_elem(p.scales, p.scale_dtype, h * p.s_sb + (kb / p.kb_per_group) * p.s_sg + n);
+        uint32_t r[64];
+        dequant_native_row<T>(p.w + (pan * p.kb + kb) * kPackedTileBytes, row, Dq<T>::from_f(sv), !p.per_channel,
+                              r);
+        uint32_t lo[32], hi[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          lo[j] = r[j];
+          hi[j] = r[32 + j];
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tmem_st32(tmem_base + lane_off + kPanelCol + 64 * kb, lo);
+        tmem_st32(tmem_base + lane_off + kPanelCol + 64 * kb + 32, hi);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&packed_empty);
-      ++runs;
-      named_bar_sync(1, 128);  // col_scale and the whole panel written by all four warps
+      tmem_st_wait();
+      tc_fence_before();
       named_bar_arrive(kPanelBar, kPanelCount);
       // 2. drain the accumulators of this run's m-tiles
-      const int n0 = nt * kBN;
       for (; i < run_end; ++i, ++tiles) {
         const int acc = tiles & 1;
         const int mt = static_cast<int>(i % p.m_tiles);
         const bool ready = mbar_wait(&acc_full[acc], static_cast<uint32_t>((tiles >> 1) & 1), abort_ptr, p.status);
         const bool live = __all_sync(0xffffffffu, ready);
         tc_fence_after();
-        const int m = mt * kBM + erow;
-        if (live) {
+        if (live) {  // warp-uniform: every lane takes part in the warp-wide tcgen05.ld
+          const long long base = h * p.out_sb + n;
 #pragma unroll 1
-          for (int c = 0; c < kBN / 16; ++c) {
+          for (int c = 0; c < kBM / 16; ++c) {
             uint32_t rr[16];
             __syncwarp();
-            tmem_ld16(tmem_base + lane_off + acc * kBN + c * 16, rr);
+            tmem_ld16(tmem_base + lane_off + acc * kBM + c * 16, rr);
             tmem_ld_wait();
-            float v[16];
+            if (n < p.N) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              v[j] = __uint_as_float(rr[j]);
-              if (p.per_channel) v[j] = __fmul_rn(v[j], col_scale[c * 16 + j]);
-            }
-            const int nc = n0 + c * 16;
-            if (m < p.M && nc < p.N) {
-              const int ncols = p.N - nc < 16 ? p.N - nc : 16;
-              store16<OUT>(p, h * p.out_sb + static_cast<long long>(m) * p.out_sm + nc, v, ncols);
+              for (int j = 0; j < 16; ++j) {
+                const int m = mt * kBM + c * 16 + j;
+                if (m < p.M) {
+                  float v = __uint_as_float(rr[j]);
+                  if (p.per_channel) v = __fmul_rn(v, col_scale);
+                  store_elem(p.out, OUT, base + static_cast<long long>(m) * p.out_sm, v);
+                }
+              }
             }
           }
         }
@@ -341,7 +305,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
       }
     }
-    if (threadIdx.x == 64) sh_packed_used = runs;
   }
 
   __syncthreads();
@@ -349,8 +312,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && abort_flag) {
       // copies issued but never consumed must land before the CTA exits
       for (int j = sh_consumed; j < sh_issued; ++j) mbar_wait(&full_bar[j % S], (j / S) & 1, nullptr, p.status);
-      for (int r = sh_packed_used; r < sh_packed_issued; ++r)
-        mbar_wait(&packed_full, static_cast<uint32_t>(r & 1), nullptr, p.status);
     }
     __syncwarp();
   }
@@ -370,8 +331,7 @@ int launch_typed(const W4A16Launch& L, cudaStream_t stream, const RParams& prm, 
   int st = encode_tmap_3d(&ta, dt, L.a, static_cast<uint64_t>(L.K), static_cast<uint64_t>(L.M),
                           static_cast<uint64_t>(L.batch), L.a_sm, L.a_sb, 64, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != CB_OK) return st;
-  const size_t smem = static_cast<size_t>(prm.kb) * (kPanelTileBytes + kPackedTileBytes) +
-                      static_cast<size_t>(prm.stages) * kBoxBytes + 1024;
+  const size_t smem = static_cast<size_t>(prm.stages) * kBoxBytes + 1024;
   static thread_local int configured_dev = -1;
   static thread_local size_t configured_smem = 0;
   int dev = 0;
@@ -427,9 +387,8 @@ int launch_w4a16_resident(const W4A16Launch& L, cudaStream_t stream) {
   const int sms = sm_count();
   if (sms <= 0) return CB_ERR_CUDA;
   const int grid = static_cast<int>(p.items < sms ? p.items : sms);
-  // ring: what is left of ~225 KiB after the panel and its packed copy
-  const size_t fixed = static_cast<size_t>(p.kb) * (kPanelTileBytes + kPackedTileBytes);
-  int stages = static_cast<int>((225u * 1024u - fixed) / kBoxBytes);
+  // ring: ~220 KiB of shared memory (the panel lives in tensor memory)
+  int stages = static_cast<int>((220u * 1024u) / kBoxBytes);
   if (stages > kMaxRingStages) stages = kMaxRingStages;
   if (stages < 2) return CB_ERR_UNSUPPORTED;
   p.stages = stages;
@@ -444,8 +403,6 @@ int launch_w4a16_resident(const W4A16Launch& L, cudaStream_t stream) {
   p.out_dtype = L.out_dtype;
   p.out_sb = L.out_sb;
   p.out_sm = L.out_sm;
-  const size_t esz = L.out_dtype == CB_DTYPE_F32 ? 4 : 2;
-  p.vec_store = aligned16(L.out) && (L.out_sm * esz) % 16 == 0 && (L.batch == 1 || (L.out_sb * esz) % 16 == 0);
   if (L.workspace == nullptr || L.workspace_bytes < kWsHeader) return CB_ERR_WORKSPACE;
   p.status = carve_workspace(L.workspace, grid).status;
   if (L.a_dtype == CB_DTYPE_BF16) return launch_out<__nv_bfloat16>(L, stream, p, grid);

@@ -28,7 +28,8 @@ from cb200 import ops  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["w8a8", "w8a8_dynamic", "w4a16", "nvfp4"], default="w8a8")
+    ap.add_argument("--op", choices=["w8a8", "w8a8_dynamic", "w4a16", "nvfp4", "mla"], default="w8a8")
+    ap.add_argument("--heads", type=int, default=16, help="mla: batch of heads (latents [heads, tokens, k])")
     ap.add_argument("--tokens", type=int, default=32)
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192)
@@ -53,6 +54,17 @@ def main():
                 ops.w8a8_gemm(q, weights[i % args.copies], s, ws_, out=out)
             else:
                 ops.w8a8_gemm_dynamic(a, weights[i % args.copies], ws_, q=q, s=s, out=out)
+    elif args.op == "mla":
+        # latent reconstruction: [heads, T, K] bf16 x int4 g128 [heads, K, N] (weight-stationary kernel)
+        H = args.heads
+        a = torch.randn(H, T, K, generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty(H, T, N, dtype=torch.bfloat16, device=dev)
+        sc = ((torch.randn(H, K // 128, N, generator=g, device=dev) * 0.02).abs() / 7 + 1e-4).to(torch.bfloat16)
+        weights = [ops.repack_w4(torch.randint(0, 256, (H, K // 2, N), generator=g, dtype=torch.uint8, device=dev),
+                                 L.CB_W4_REF_U8_KN, K, N) for _ in range(args.copies)]
+
+        def run(i):
+            ops.w4a16_gemm(a, weights[i % args.copies], sc, N, 128, out=out)
     elif args.op == "nvfp4":
         gx = torch.tensor([448.0 * 6.0 / float(a.float().abs().max())], device=dev)
         qa, sa = ops.nvfp4_quantize(a, gx)
