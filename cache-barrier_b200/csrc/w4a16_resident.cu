@@ -23,9 +23,13 @@
 //      (N = 128 tokens), fp32 accumulators [128 columns x 128 tokens] in TMEM,
 //      double-buffered across m-tiles;
 //   3. warps 2-5 convert each finished accumulator (per-channel scale applied
-//      in fp32 here when G >= K): the thread of lane n stores output column n
-//      for the tile's 128 tokens, so each store of a warp covers 32 adjacent
-//      columns of one token row.
+//      in fp32 here when G >= K). The thread of lane n holds output column n
+//      for the tile's 128 tokens; for 16-bit outputs (N % 8 == 0, 16-byte
+//      aligned rows) each warp stages 16 tokens x its 32 columns in shared
+//      memory and writes them back as 16-byte vectors of 8 columns, one eighth
+//      of the store instructions of column-per-thread 2-byte stores (those
+//      made the epilogue, at ~8K cycles per m-tile, the kernel's limit);
+//      otherwise each thread stores its column element by element.
 // Runs that start a new panel wait until the previous panel's MMAs are done
 // (its last accumulator was drained) before overwriting it.
 #include <cuda.h>
@@ -56,6 +60,8 @@ constexpr uint32_t kPackedTileBytes = kBN * kBK / 2;
 constexpr uint32_t kPanelCol = 2 * kBM;           // after two accumulators of 128 fp32 columns
 constexpr uint32_t kTmemCols = 512;               // + the panel: 64 columns per 128 k, K <= 512
 constexpr int kMaxRingStages = 16;
+constexpr uint32_t kStageTileBytes = 16 * 32 * 2;  // per epilogue warp: 16 tokens x 32 columns, 16-bit
+constexpr uint32_t kEpiStageBytes = 4 * kStageTileBytes;
 
 struct RParams {
   int M, N, K, H;
@@ -71,6 +77,7 @@ struct RParams {
   void* out;
   int out_dtype;
   long long out_sb, out_sm;
+  int vec_out;                // 16-bit output, N % 8 == 0, 16-byte aligned rows: vector stores
   int* status;
 };
 
@@ -93,6 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;  // stages x 16 KiB activation boxes
+  uint16_t* epi_stage = reinterpret_cast<uint16_t*>(smem + p.stages * kBoxBytes);  // 4 x 1 KiB
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -279,7 +287,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool ready = mbar_wait(&acc_full[acc], static_cast<uint32_t>((tiles >> 1) & 1), abort_ptr, p.status);
         const bool live = __all_sync(0xffffffffu, ready);
         tc_fence_after();
-        if (live) {  // warp-uniform: every lane takes part in the warp-wide tcgen05.ld
+        if (live && OUT != CB_DTYPE_F32 && p.vec_out) {  // warp-uniform (tcgen05.ld is warp-wide)
+          uint16_t* stg = epi_stage + (warp - 2) * (kStageTileBytes / 2);
+          const int q8 = lane & 3;  // 8-column chunk of this warp's 32 columns
+          const int n8 = nt * kBN + quarter * 32 + q8 * 8;
+          uint16_t* out16 = static_cast<uint16_t*>(p.out) + h * p.out_sb + n8;
+#pragma unroll 1
+          for (int c = 0; c < kBM / 16; ++c) {
+            uint32_t rr[16];
+            __syncwarp();
+            tmem_ld16(tmem_base + lane_off + acc * kBM + c * 16, rr);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float v = __uint_as_float(rr[j]);
+              if (p.per_channel) v = __fmul_rn(v, col_scale);
+              const uint16_t b = OUT == CB_DTYPE_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
+                                                      : __half_as_ushort(__float2half_rn(v));
+              stg[j * 32 + lane] = b;  // token j, column lane
+            }
+            __syncwarp();
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+              const int jt = (lane >> 2) + 8 * r;
+              const int m = mt * kBM + c * 16 + jt;
+              const uint4 v = *reinterpret_cast<const uint4*>(stg + jt * 32 + q8 * 8);
+              if (m < p.M && n8 < p.N) *reinterpret_cast<uint4*>(out16 + static_cast<long long>(m) * p.out_sm) = v;
+            }
+          }
+          __syncwarp();
+        } else if (live) {  // warp-uniform: every lane takes part in the warp-wide tcgen05.ld
           const long long base = h * p.out_sb + n;
 #pragma unroll 1
           for (int c = 0; c < kBM / 16; ++c) {
@@ -331,7 +368,7 @@ int launch_typed(const W4A16Launch& L, cudaStream_t stream, const RParams& prm, 
   int st = encode_tmap_3d(&ta, dt, L.a, static_cast<uint64_t>(L.K), static_cast<uint64_t>(L.M),
                           static_cast<uint64_t>(L.batch), L.a_sm, L.a_sb, 64, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != CB_OK) return st;
-  const size_t smem = static_cast<size_t>(prm.stages) * kBoxBytes + 1024;
+  const size_t smem = static_cast<size_t>(prm.stages) * kBoxBytes + kEpiStageBytes + 1024;
   static thread_local int configured_dev = -1;
   static thread_local size_t configured_smem = 0;
   int dev = 0;
@@ -388,7 +425,7 @@ int launch_w4a16_resident(const W4A16Launch& L, cudaStream_t stream) {
   if (sms <= 0) return CB_ERR_CUDA;
   const int grid = static_cast<int>(p.items < sms ? p.items : sms);
   // ring: ~220 KiB of shared memory (the panel lives in tensor memory)
-  int stages = static_cast<int>((220u * 1024u) / kBoxBytes);
+  int stages = static_cast<int>((220u * 1024u - kEpiStageBytes) / kBoxBytes);
   if (stages > kMaxRingStages) stages = kMaxRingStages;
   if (stages < 2) return CB_ERR_UNSUPPORTED;
   p.stages = stages;
@@ -403,6 +440,10 @@ int launch_w4a16_resident(const W4A16Launch& L, cudaStream_t stream) {
   p.out_dtype = L.out_dtype;
   p.out_sb = L.out_sb;
   p.out_sm = L.out_sm;
+  p.vec_out = (L.out_dtype != CB_DTYPE_F32 && L.N % 8 == 0 && aligned16(L.out) && L.out_sm % 8 == 0 &&
+               (L.batch == 1 || L.out_sb % 8 == 0))
+                  ? 1
+                  : 0;
   if (L.workspace == nullptr || L.workspace_bytes < kWsHeader) return CB_ERR_WORKSPACE;
   p.status = carve_workspace(L.workspace, grid).status;
   if (L.a_dtype == CB_DTYPE_BF16) return launch_out<__nv_bfloat16>(L, stream, p, grid);
