@@ -246,7 +246,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- dequant + epilogue (warps 2-5) ----------------
     // Control flow is uniform: after a failed wait the work is skipped but every
     // arrival still happens.
-    pdl_wait_primary();  // the output may still be read by the preceding kernel
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // TMEM lane = panel row = output column within the panel
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
@@ -259,28 +258,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = nt * kBN + row;
       // 1. dequantize the panel into tensor memory (the previous run's MMAs
       //    are done: its last accumulator was drained below before this point)
+      // All of the row's packed bytes (K <= 512: at most 4 x 64 bytes) and group
+      // scales are loaded before the first tensor-memory store: the stores'
+      // ordering would otherwise keep each k-tile's loads behind the previous
+      // k-tile's, one global round trip per k-tile before the first MMA.
       float col_scale = 1.0f;
       if (p.per_channel && n < p.N) col_scale = load_elem(p.scales, p.scale_dtype, h * p.s_sb + n);
-      for (int kb = 0; kb < p.kb; ++kb) {
-        float sv = 1.0f;
-        if (!p.per_channel && n < p.N)
-          sv = load_elem(p.scales, p.scale_dtype, h * p.s_sb + (kb / p.kb_per_group) * p.s_sg + n);
-        uint32_t r[64];
-        dequant_native_row<T>(p.w + (pan * p.kb + kb) * kPackedTileBytes, row, Dq<T>::from_f(sv), !p.per_channel,
-                              r);
-        uint32_t lo[32], hi[32];
+      uint4 raw[kMaxKB][4];
+      float svs[kMaxKB];
+      const int swz = (row >> 1) & 3;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          lo[j] = r[j];
-          hi[j] = r[32 + j];
+      for (int kb = 0; kb < kMaxKB; ++kb) {
+        svs[kb] = 1.0f;
+        if (kb < p.kb) {
+          if (!p.per_channel && n < p.N)
+            svs[kb] = load_elem(p.scales, p.scale_dtype, h * p.s_sb + (kb / p.kb_per_group) * p.s_sg + n);
+          const uint4* wrow = reinterpret_cast<const uint4*>(p.w + (pan * p.kb + kb) * kPackedTileBytes + row * 64);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) raw[kb][c] = __ldg(wrow + (c ^ swz));
         }
-        tmem_st32(tmem_base + lane_off + kPanelCol + 64 * kb, lo);
-        tmem_st32(tmem_base + lane_off + kPanelCol + 64 * kb + 32, hi);
+      }
+      const typename Dq<T>::T2 bias = Dq<T>::bias();
+#pragma unroll
+      for (int kb = 0; kb < kMaxKB; ++kb) {
+        if (kb < p.kb) {
+          const typename Dq<T>::T2 sc = Dq<T>::from_f(svs[kb]);
+          uint32_t lo[32], hi[32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t words[4] = {raw[kb][c].x, raw[kb][c].y, raw[kb][c].z, raw[kb][c].w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+              for (int pi = 0; pi < 4; ++pi) {
+                const uint32_t v = dq_pair<T>(words[wi], 4 * pi, bias, sc, !p.per_channel);
+                const int idx = c * 16 + wi * 4 + pi;  // pair index: k = 2 idx, 2 idx + 1
+                if (idx < 32)
+                  lo[idx] = v;
+                else
+                  hi[idx - 32] = v;
+              }
+          }
+          tmem_st32(tmem_base + lane_off + kPanelCol + 64 * kb, lo);
+          tmem_st32(tmem_base + lane_off + kPanelCol + 64 * kb + 32, hi);
+        }
       }
       tmem_st_wait();
       tc_fence_before();
       named_bar_arrive(kPanelBar, kPanelCount);
-      // 2. drain the accumulators of this run's m-tiles
+      // 2. drain the accumulators of this run's m-tiles. The panel above is
+      //    weights only, so it was built while the preceding kernel finished;
+      //    the output may still be read by that kernel until this wait.
+      pdl_wait_primary();
       for (; i < run_end; ++i, ++tiles) {
         const int acc = tiles & 1;
         const int mt = static_cast<int>(i % p.m_tiles);
