@@ -147,6 +147,7 @@ struct Params {
   void* out;
   int out_dtype;
   long long out_sm;
+  int vec_out;  // 16-bit output, N % 8 == 0, 16-byte aligned rows: vector stores
   float* partials;  // [grid][2][TN][128]
   int* counters;
   int* status;
@@ -167,6 +168,33 @@ __device__ __forceinline__ void sum_published(const Params& p, int c_lo, int c_h
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], part[j]);
   }
+}
+
+// emit_row for 16-bit outputs through shared memory: the warp stages its 32
+// columns x 16 tokens (thread = column) and stores them back as 16-byte vectors
+// of 8 columns, one eighth of the store instructions. Same arithmetic and
+// rounding as emit_row.
+template <int OUT_BF16>
+__device__ __forceinline__ void emit_chunk_vec(const Params& p, int n_warp0, int lane, int m0, int t0,
+                                               const float (&v)[16], float alpha, uint16_t* stg) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float f = __fmul_rn(v[j], alpha);
+    stg[j * 32 + lane] =
+        OUT_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(f)) : __half_as_ushort(__float2half_rn(f));
+  }
+  __syncwarp();
+  const int q8 = lane & 3;
+  const int n8 = n_warp0 + q8 * 8;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int jt = (lane >> 2) + 8 * r;
+    const int m = m0 + t0 + jt;
+    const uint4 val = *reinterpret_cast<const uint4*>(stg + jt * 32 + q8 * 8);
+    if (m < p.M && n8 < p.N)
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + static_cast<long long>(m) * p.out_sm + n8) = val;
+  }
+  __syncwarp();
 }
 
 __device__ __forceinline__ void emit_row(const Params& p, int n, int m0, int t0, const float (&v)[16], float alpha) {
@@ -206,6 +234,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem_x = smem + S * kWTileBytes;
   uint8_t* smem_sfw = smem_x + S * kXTileBytes;
   uint8_t* smem_sfx = smem_sfw + S * kSfStage;
+  // per epilogue warp: 16 tokens x 32 columns of 16-bit output (vector-store staging)
+  uint16_t* epi_stage = reinterpret_cast<uint16_t*>(smem_sfx + S * kSfStage);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -458,10 +488,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = nt * kBlockN + row;
       const int m0 = mt * TN;
       bool others_ready = true;
+      // The collector sums the other contributors' parts (in CTA order) while
+      // its own last MMAs still run, then adds its accumulator.
+      constexpr bool kPrefetch = TN <= 32;
+      float other[kPrefetch ? TN : 1];
       if (collect) {
         if (threadIdx.x == 64) sh_is_last = wait_counter(&p.counters[c_first], c_last - c_first, abort_ptr, p.status);
         named_bar_sync(1, 128);
         others_ready = sh_is_last != 0;
+        if constexpr (kPrefetch) {
+#pragma unroll
+          for (int c = 0; c < TN / 16; ++c) {
+            float t[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) t[j] = 0.0f;
+            if (others_ready) sum_published<TN>(p, c_first + 1, c_last, c, row, t);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) other[c * 16 + j] = t[j];
+          }
+          // Complete the loads now, not at their use after the accumulator wait.
+#pragma unroll
+          for (int j = 0; j < TN; ++j) asm volatile("" ::"f"(other[j]));
+        }
       }
       const bool got = mbar_wait(&tfull_bar, acc_phase, abort_ptr, p.status);
       acc_phase ^= 1u;
@@ -469,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       if (whole || collect) {
         if (live && others_ready) {
-#pragma unroll 1
+#pragma unroll
           for (int c = 0; c < TN / 16; ++c) {
             uint32_t r[16];
             __syncwarp();
@@ -478,8 +526,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             float v[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-            if (collect) sum_published<TN>(p, c_first + 1, c_last, c, row, v);
-            emit_row(p, n, m0, c * 16, v, alpha);
+            if (collect) {
+              if constexpr (kPrefetch) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], other[c * 16 + j]);
+              } else {
+                sum_published<TN>(p, c_first + 1, c_last, c, row, v);
+              }
+            }
+            if (p.vec_out) {
+              uint16_t* stg = epi_stage + (warp - 2) * 512;
+              if (p.out_dtype == CB_DTYPE_BF16)
+                emit_chunk_vec<1>(p, n - lane, lane, m0, c * 16, v, alpha, stg);
+              else
+                emit_chunk_vec<0>(p, n - lane, lane, m0, c * 16, v, alpha, stg);
+            } else {
+              emit_row(p, n, m0, c * 16, v, alpha);
+            }
           }
           if (collect && threadIdx.x == 64) p.counters[c_first] = 0;  // next launch starts from zero
         }
@@ -542,7 +605,7 @@ int launch_tn(const Nvfp4Launch& L, cudaStream_t stream, int grid, const Params&
                       CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != CB_OK) return st;
   const size_t stage_bytes = kWTileBytes + static_cast<size_t>(TN) * kStageRowBytes + 2 * kSfStage;
-  const size_t smem = static_cast<size_t>(prm.stages) * stage_bytes + 1024;
+  const size_t smem = static_cast<size_t>(prm.stages) * stage_bytes + 4 * 1024 + 1024;
   static thread_local int configured_dev = -1;
   static thread_local size_t configured_smem = 0;
   int dev = 0;
@@ -641,6 +704,10 @@ int launch_nvfp4_gemm(const Nvfp4Launch& L, cudaStream_t stream) {
   p.out = L.out;
   p.out_dtype = L.out_dtype;
   p.out_sm = L.out_sm;
+  p.vec_out = ((L.out_dtype == CB_DTYPE_BF16 || L.out_dtype == CB_DTYPE_F16) && L.N % 8 == 0 && aligned16(L.out) &&
+               L.out_sm % 8 == 0)
+                  ? 1
+                  : 0;
   Workspace ws = carve_workspace(L.workspace, grid);
   p.partials = static_cast<float*>(ws.partials);
   p.counters = ws.counters;
