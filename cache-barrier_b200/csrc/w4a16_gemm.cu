@@ -74,6 +74,7 @@ struct Params {
   void* out;
   int out_dtype;
   long long out_sb, out_sm;
+  int vec_out;  // 16-bit output, N % 8 == 0, 16-byte aligned rows: vector stores
   float* partials;  // [grid][2][TN][128]
   int* counters;
   int* status;
@@ -97,6 +98,48 @@ __device__ __forceinline__ void emit_row(const Params& p, int h, int n, int m0, 
       const float f = p.scale_in_epilogue ? __fmul_rn(v[j], sc) : v[j];
       store_elem(p.out, p.out_dtype, idx, f);
     }
+  }
+}
+
+// emit_row for 16-bit outputs through shared memory: the warp stages its 32
+// columns x 16 tokens (thread = column) and stores them back as 16-byte vectors
+// of 8 columns, one eighth of the store instructions. Same arithmetic and
+// rounding as emit_row.
+template <int OUT_BF16>
+__device__ __forceinline__ void emit_chunk_vec(const Params& p, int h, int n, int lane, int m0, int t0,
+                                               const float (&v)[16], uint16_t* stg) {
+  const float sc = (p.scale_in_epilogue && n < p.N) ? load_elem(p.scales, p.scale_dtype, h * p.s_sb + n) : 1.0f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float f = p.scale_in_epilogue ? __fmul_rn(v[j], sc) : v[j];
+    stg[j * 32 + lane] =
+        OUT_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(f)) : __half_as_ushort(__float2half_rn(f));
+  }
+  __syncwarp();
+  const int q8 = lane & 3;
+  const int n8 = n - lane + q8 * 8;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int jt = (lane >> 2) + 8 * r;
+    const int m = m0 + t0 + jt;
+    const uint4 val = *reinterpret_cast<const uint4*>(stg + jt * 32 + q8 * 8);
+    if (m < p.M && n8 < p.N)
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + h * p.out_sb + static_cast<long long>(m) * p.out_sm +
+                                n8) = val;
+  }
+  __syncwarp();
+}
+
+// Warp-collective store of one 16-token chunk (every lane of the warp calls it).
+__device__ __forceinline__ void emit_chunk(const Params& p, int h, int n, int lane, int m0, int t0,
+                                           const float (&v)[16], uint16_t* stg) {
+  if (p.vec_out) {
+    if (p.out_dtype == CB_DTYPE_BF16)
+      emit_chunk_vec<1>(p, h, n, lane, m0, t0, v, stg);
+    else
+      emit_chunk_vec<0>(p, h, n, lane, m0, t0, v, stg);
+  } else {
+    emit_row(p, h, n, m0, t0, v);
   }
 }
 
@@ -144,6 +187,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem_abuf = smem;                                  // dequantized A tiles (1024-aligned)
   uint8_t* smem_a = smem + kNumABuf * kABufBytes;             // token tiles (1024-aligned)
   uint8_t* smem_w = smem_a + p.stages * kATileBytes;          // packed weight tiles
+  // per epilogue warp: 16 tokens x 32 columns of 16-bit output (vector-store staging)
+  uint16_t* epi_stage = reinterpret_cast<uint16_t*>(smem_w + p.stages * kWTileBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -479,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float v[16];
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) v[jj] = __uint_as_float(r[jj]);
-            emit_row(p, h, n, m0, c * 16, v);
+            emit_chunk(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - kEpiWarp0) * 512);
           }
         }
         tc_fence_before();
@@ -519,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               float v[16];
 #pragma unroll
               for (int jj = 0; jj < 16; ++jj) v[jj] = __fadd_rn(__uint_as_float(r[jj]), other[c * 16 + jj]);
-              emit_row(p, h, n, m0, c * 16, v);
+              emit_chunk(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - kEpiWarp0) * 512);
             }
           } else {
 #pragma unroll 1
@@ -532,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int jj = 0; jj < 16; ++jj) v[jj] = __uint_as_float(r[jj]);
               sum_published<TN>(p, c_first + 1, c_last, c, row, v);
-              emit_row(p, h, n, m0, c * 16, v);
+              emit_chunk(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - kEpiWarp0) * 512);
             }
           }
           if (threadIdx.x == kEpiThread0) p.counters[c_first] = 0;  // next launch starts from zero
@@ -568,7 +613,8 @@ int launch_typed(const W4A16Launch& L, cudaStream_t stream, int grid, int stages
   int st = encode_tmap_3d(&ta, dt, L.a, static_cast<uint64_t>(L.K), static_cast<uint64_t>(L.M),
                           static_cast<uint64_t>(L.batch), L.a_sm, L.a_sb, 64, TN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != CB_OK) return st;
-  const size_t smem = kNumABuf * kABufBytes + static_cast<size_t>(stages) * (kWTileBytes + TN * kBlockK * 2) + 1024;
+  const size_t smem =
+      kNumABuf * kABufBytes + static_cast<size_t>(stages) * (kWTileBytes + TN * kBlockK * 2) + 4 * 1024 + 1024;
   static thread_local int configured_dev = -1;
   static thread_local size_t configured_smem = 0;
   int dev = 0;
@@ -660,6 +706,10 @@ int launch_w4a16(const W4A16Launch& L, cudaStream_t stream) {
   p.out_dtype = L.out_dtype;
   p.out_sb = L.out_sb;
   p.out_sm = L.out_sm;
+  p.vec_out = ((L.out_dtype == CB_DTYPE_BF16 || L.out_dtype == CB_DTYPE_F16) && L.N % 8 == 0 && aligned16(L.out) &&
+               L.out_sm % 8 == 0 && (L.batch == 1 || L.out_sb % 8 == 0))
+                  ? 1
+                  : 0;
   Workspace ws = carve_workspace(L.workspace, grid);
   p.partials = static_cast<float*>(ws.partials);
   p.counters = ws.counters;
