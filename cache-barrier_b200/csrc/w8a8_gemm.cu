@@ -140,6 +140,29 @@ __device__ __forceinline__ void emit_chunk_vec(const Params& p, int h, int n_war
   __syncwarp();
 }
 
+// Warp-collective store of one 16-token chunk for the paths without preloaded
+// scales (token tiles above 32): loads the scales as emit_row does, then takes
+// the vector path for 16-bit outputs.
+template <int TN>
+__device__ __forceinline__ void emit_row_any(const Params& p, int h, int n, int lane, int m0, int t0,
+                                             const int32_t (&v)[16], uint16_t* stg) {
+  if (!p.vec_out) {
+    emit_row<TN>(p, h, n, m0, t0, v);
+    return;
+  }
+  const float ws = n < p.N ? __ldg(p.w_scale + h * p.ws_sb + n) : 1.0f;
+  float as[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int m = m0 + t0 + j;
+    as[j] = m < p.M ? __ldg(p.a_scale + h * p.as_sb + m) : 1.0f;
+  }
+  if (p.out_dtype == CB_DTYPE_BF16)
+    emit_chunk_vec<1>(p, h, n - lane, lane, m0, t0, v, ws, as, stg);
+  else
+    emit_chunk_vec<0>(p, h, n - lane, lane, m0, t0, v, ws, as, stg);
+}
+
 // Adds the published parts of contributors [c_lo, c_hi] (each its first
 // segment, slot kind 0) for chunk c of this thread's row; loads of four
 // contributors are in flight together.
@@ -471,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               int32_t v[16];
 #pragma unroll
               for (int j = 0; j < 16; ++j) v[j] = static_cast<int32_t>(r[j]);
-              emit_row<TN>(p, h, n, m0, c * 16, v);
+              emit_row_any<TN>(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - 2) * 512);
             }
           }
         }
@@ -539,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) v[j] = static_cast<int32_t>(r[j]);
               sum_published<TN>(p, c_first + 1, c_last, c, row, v);
-              emit_row<TN>(p, h, n, m0, c * 16, v);
+              emit_row_any<TN>(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - 2) * 512);
             }
           }
           if (threadIdx.x == 64) p.counters[c_first] = 0;  // next launch starts from zero
