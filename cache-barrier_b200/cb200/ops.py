@@ -171,13 +171,14 @@ def rmsnorm_quant_i8(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, q
 # ---------------------------------------------------------------------------
 def w8a8_gemm(aq: torch.Tensor, w_nk: torch.Tensor, a_scale: torch.Tensor, w_scale: torch.Tensor,
               out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
-              acc_out: torch.Tensor | None = None) -> torch.Tensor:
-    """``out = (aq @ w_nk^T)_int32 * a_scale[m] * w_scale[n]``.
+              acc_out: torch.Tensor | None = None, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """``out = (aq @ w_nk^T)_int32 * a_scale[m] * w_scale[n] (+ bias[n])``.
 
     aq: int8 [M, K] / [B, M, K]; w_nk: int8 [N, K] / [B, N, K] (K contiguous);
-    a_scale: fp32 with B*M elements; w_scale: fp32 [N] / [B, N].
+    a_scale: fp32 with B*M elements; w_scale: fp32 [N] / [B, N]; bias (optional):
+    f16/bf16/f32 [N] / [B, N], added in fp32 before the output rounding.
     """
-    _require_cuda(aq, w_nk, a_scale, w_scale, out, acc_out)
+    _require_cuda(aq, w_nk, a_scale, w_scale, out, acc_out, bias)
     a3, w3 = _as3d(aq), _as3d(w_nk)
     B, M, K = a3.shape
     Bw, N, Kw = w3.shape
@@ -204,14 +205,27 @@ def w8a8_gemm(aq: torch.Tensor, w_nk: torch.Tensor, a_scale: torch.Tensor, w_sca
         acc3 = _as3d(acc_out)
         if acc_out.dtype != torch.int32 or acc3.shape != o3.shape or acc3.stride() != o3.stride():
             raise ValueError("acc_out must be int32 with out's shape and strides")
+    b2, b_sb = None, 0
+    if bias is not None:
+        b2 = bias.reshape(1, N) if bias.dim() == 1 else bias
+        if b2.shape[-1] != N or b2.stride(-1) != 1 or b2.shape[0] not in (1, B):
+            raise ValueError("bias must be [N] or [B, N], contiguous along N")
+        b_sb = b2.stride(0) if b2.shape[0] == B and B > 1 else 0
+        dtype_code(bias.dtype)
     nbytes = workspace_bytes(L.CB_OP_W8A8, B, M, N, K)
     ws = POOL.get(nbytes, aq.device)
     st = _strides(a3.stride(0), a3.stride(1), w3.stride(0), w3.stride(1), o3.stride(0), o3.stride(1), M,
                   ws2.stride(0) if ws2.dim() == 2 else 0)
-    code = L.load().cb_w8a8_gemm(a3.data_ptr(), a_scale.data_ptr(), w3.data_ptr(), ws2.data_ptr(), o3.data_ptr(),
-                                 dtype_code(out.dtype), _ptr(acc3), B, M, N, K, st, ws.data_ptr(), ws.numel(),
-                                 _stream(aq.device))
-    L.check("cb_w8a8_gemm", code)
+    if b2 is None:
+        code = L.load().cb_w8a8_gemm(a3.data_ptr(), a_scale.data_ptr(), w3.data_ptr(), ws2.data_ptr(), o3.data_ptr(),
+                                     dtype_code(out.dtype), _ptr(acc3), B, M, N, K, st, ws.data_ptr(), ws.numel(),
+                                     _stream(aq.device))
+        L.check("cb_w8a8_gemm", code)
+        return out
+    code = L.load().cb_w8a8_gemm_bias(a3.data_ptr(), a_scale.data_ptr(), w3.data_ptr(), ws2.data_ptr(), b2.data_ptr(),
+                                      dtype_code(b2.dtype), b_sb, o3.data_ptr(), dtype_code(out.dtype), _ptr(acc3), B,
+                                      M, N, K, st, ws.data_ptr(), ws.numel(), _stream(aq.device))
+    L.check("cb_w8a8_gemm_bias", code)
     return out
 
 

@@ -4,12 +4,19 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "cb200.h"
 #include "cb_internal.h"
 
 namespace cb {
+
+namespace {
+std::atomic<unsigned long long> g_debug_wait_ns{0};
+}  // namespace
+
+unsigned long long debug_wait_ns() { return g_debug_wait_ns.load(std::memory_order_relaxed); }
 
 int sm_count() {
   static int cached[64] = {0};
@@ -203,6 +210,21 @@ int validate_w8a8(const int8_t* aq, const int8_t* w, void* out, int out_dtype, i
   return CB_OK;
 }
 
+int read_and_clear_status(void* scratch, int* device_status, cudaStream_t s) {
+  int host = 0;
+  if (cudaMemcpyAsync(&host, scratch, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return CB_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return CB_ERR_CUDA;
+  if (device_status) *device_status = host;
+  if (host != 0) {
+    // A kernel that gave up a wait may have left arrival counters behind: clear
+    // them with the status word so the next call starts from zero.
+    if (cudaMemsetAsync(scratch, 0, kWsHeader + kWsCounters, s) != cudaSuccess) return CB_ERR_CUDA;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return CB_ERR_CUDA;
+    return CB_ERR_DEVICE_TIMEOUT;
+  }
+  return CB_OK;
+}
+
 }  // namespace cb
 
 using namespace cb;
@@ -264,16 +286,11 @@ size_t cb_workspace_bytes(int op, int64_t batch, int64_t M, int64_t N, int64_t K
 
 int cb_workspace_status(void* workspace, int* device_status, cb_stream_t stream) {
   if (!workspace) return CB_ERR_INVALID_ARG;
-  int host = 0;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (cudaMemcpyAsync(&host, workspace, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return CB_ERR_CUDA;
-  if (cudaStreamSynchronize(s) != cudaSuccess) return CB_ERR_CUDA;
-  if (device_status) *device_status = host;
-  if (host != 0) {
-    if (cudaMemsetAsync(workspace, 0, sizeof(int), s) != cudaSuccess) return CB_ERR_CUDA;
-    return CB_ERR_DEVICE_TIMEOUT;
-  }
-  return CB_OK;
+  return read_and_clear_status(workspace, device_status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+void cb_debug_force_wait_timeout(uint64_t limit_ns) {
+  g_debug_wait_ns.store(static_cast<unsigned long long>(limit_ns), std::memory_order_relaxed);
 }
 
 int cb_quant_act_i8(const void* a, int a_dtype, int64_t batch, int64_t M, int64_t K, int64_t a_stride_b,
@@ -291,9 +308,19 @@ int cb_quant_act_i8(const void* a, int a_dtype, int64_t batch, int64_t M, int64_
 int cb_w8a8_gemm(const int8_t* aq, const float* a_scale, const int8_t* w, const float* w_scale, void* out,
                  int out_dtype, int32_t* acc_out, int64_t batch, int64_t M, int64_t N, int64_t K,
                  const int64_t* strides, void* workspace, size_t workspace_bytes, cb_stream_t stream) {
+  return cb_w8a8_gemm_bias(aq, a_scale, w, w_scale, nullptr, CB_DTYPE_F32, 0, out, out_dtype, acc_out, batch, M, N,
+                           K, strides, workspace, workspace_bytes, stream);
+}
+
+int cb_w8a8_gemm_bias(const int8_t* aq, const float* a_scale, const int8_t* w, const float* w_scale,
+                      const void* bias, int bias_dtype, int64_t bias_stride_b, void* out, int out_dtype,
+                      int32_t* acc_out, int64_t batch, int64_t M, int64_t N, int64_t K, const int64_t* strides,
+                      void* workspace, size_t workspace_bytes, cb_stream_t stream) {
   int v = validate_w8a8(aq, w, out, out_dtype, batch, M, N, K, strides);
   if (v != CB_OK || batch * M * N == 0) return v;
   if (!a_scale || !w_scale) return CB_ERR_INVALID_ARG;
+  if (bias && !valid_out_dtype(bias_dtype)) return CB_ERR_DTYPE;
+  if (bias && batch > 1 && bias_stride_b < N) return CB_ERR_STRIDE;
   W8A8Launch L = {};
   L.aq = aq;
   L.a_scale = a_scale;
@@ -315,6 +342,9 @@ int cb_w8a8_gemm(const int8_t* aq, const float* a_scale, const int8_t* w, const 
   L.as_sb = strides[6];
   L.ws_sb = strides[7];
   L.raw_f32 = 0;
+  L.bias = bias;
+  L.bias_dtype = bias_dtype;
+  L.bias_sb = bias_stride_b;
   L.workspace = workspace;
   L.workspace_bytes = workspace_bytes;
   return launch_w8a8(L, reinterpret_cast<cudaStream_t>(stream));

@@ -12,7 +12,13 @@
 namespace cb {
 
 constexpr int kMaxStages = 16;
-constexpr size_t kWsHeader = 256;  // status word + padding
+// Workspace header: word 0 is the status word; word 1 is never written (the
+// failure-detection test hook waits on it); the rest is padding.
+constexpr size_t kWsHeader = 256;
+
+// Wait limit of the failure-detection test hook (0 = off), set by
+// cb_debug_force_wait_timeout and read by the W8A8 launcher.
+unsigned long long debug_wait_ns();
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -73,6 +79,11 @@ int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
 
 inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? CB_OK : CB_ERR_CUDA; }
 
+// Synchronizing read of the status word at the start of a workspace (or of the
+// no-alloc scratch array); on a recorded timeout it clears the word and the
+// arrival counters and returns CB_ERR_DEVICE_TIMEOUT.
+int read_and_clear_status(void* scratch, int* device_status, cudaStream_t s);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Argument checks shared by the W8A8 entry points (strides as in cb_w8a8_gemm).
@@ -95,6 +106,9 @@ struct W8A8Launch {
   int64_t aq_sb, aq_sm, w_sb, w_sn, out_sb, out_sm, as_sb, ws_sb;
   int raw_f32;            // 1: out = (float)acc, no scales (W4A4 path)
   int unsigned_operands;  // 1: both operands are uint8 (W4A4 reference-wrap mode)
+  const void* bias;       // optional [batch, N] bias (f16/bf16/f32) added in fp32 before rounding
+  int bias_dtype;
+  int64_t bias_sb;
   void* workspace;
   size_t workspace_bytes;
 };

@@ -91,14 +91,17 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
 }
 
 // Bounded wait until *ctr >= target (another CTA of the same grid publishes it).
-__device__ __forceinline__ bool wait_counter(const int* ctr, int target, volatile int* abort_flag, int* status) {
+// limit_ns defaults to kWaitLimitNs; the failure-detection test hook passes a
+// short one.
+__device__ __forceinline__ bool wait_counter(const int* ctr, int target, volatile int* abort_flag, int* status,
+                                             unsigned long long limit_ns = kWaitLimitNs) {
   if (ld_acquire_gpu(ctr) >= target) return true;
   const unsigned long long t0 = global_timer_ns();
   while (true) {
     __nanosleep(64);
     if (ld_acquire_gpu(ctr) >= target) return true;
     if (abort_flag && *abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       if (abort_flag) *abort_flag = 1;
       if (status) atomicOr(status, CB_DEVERR_TIMEOUT);
       return false;

@@ -54,6 +54,10 @@ struct Params {
   long long out_sb, out_sm;
   int32_t* acc_out;
   int raw_f32;
+  const void* bias;  // optional per-output-channel bias, added in fp32 before the rounding
+  int bias_dtype;
+  long long bias_sb;
+  unsigned long long dbg_wait_ns;  // test hook: nonzero = wait this long on a flag nothing sets
   int vec_out;  // 16-bit output, N % 8 == 0, 16-byte aligned rows, no acc_out: vector stores
   int32_t* partials;  // [grid][2][TN][128]
   int* counters;      // [grid]
@@ -73,6 +77,7 @@ __device__ __forceinline__ void emit_row(const Params& p, int h, int n, int m0, 
   // All scale loads are issued before any store: a load placed after a store
   // that may alias it would otherwise wait for the previous iteration.
   const float ws = p.raw_f32 ? 1.0f : __ldg(p.w_scale + h * p.ws_sb + n);
+  const float bv = p.bias ? load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n) : 0.0f;
   float as[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
@@ -86,15 +91,16 @@ __device__ __forceinline__ void emit_row(const Params& p, int h, int n, int m0, 
       const long long idx = h * p.out_sb + static_cast<long long>(m) * p.out_sm + n;
       float f = __int2float_rn(v[j]);
       if (!p.raw_f32) f = __fmul_rn(__fmul_rn(f, as[j]), ws);
+      if (p.bias) f = __fadd_rn(f, bv);
       store_elem(p.out, p.out_dtype, idx, f);
       if (p.acc_out) p.acc_out[idx] = v[j];
     }
   }
 }
 
-// emit_row with the scales already in registers (loaded when the segment began).
+// emit_row with the scales (and bias) already in registers (loaded when the segment began).
 __device__ __forceinline__ void emit_row_pre(const Params& p, int h, int n, int m0, int t0, const int32_t (&v)[16],
-                                             float ws, const float (&as)[16]) {
+                                             float ws, float bv, const float (&as)[16]) {
   if (n >= p.N) return;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
@@ -103,6 +109,7 @@ __device__ __forceinline__ void emit_row_pre(const Params& p, int h, int n, int 
       const long long idx = h * p.out_sb + static_cast<long long>(m) * p.out_sm + n;
       float f = __int2float_rn(v[j]);
       if (!p.raw_f32) f = __fmul_rn(__fmul_rn(f, as[j]), ws);
+      if (p.bias) f = __fadd_rn(f, bv);
       store_elem(p.out, p.out_dtype, idx, f);
       if (p.acc_out) p.acc_out[idx] = v[j];
     }
@@ -117,11 +124,13 @@ __device__ __forceinline__ void emit_row_pre(const Params& p, int h, int n, int 
 // Same arithmetic and rounding as emit_row_pre.
 template <int OUT_BF16>
 __device__ __forceinline__ void emit_chunk_vec(const Params& p, int h, int n_warp0, int lane, int m0, int t0,
-                                               const int32_t (&v)[16], float ws, const float (&as)[16],
+                                               const int32_t (&v)[16], float ws, float bv, const float (&as)[16],
                                                uint16_t* stg) {
+  const bool has_bias = p.bias != nullptr;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const float f = __fmul_rn(__fmul_rn(__int2float_rn(v[j]), as[j]), ws);
+    float f = __fmul_rn(__fmul_rn(__int2float_rn(v[j]), as[j]), ws);
+    if (has_bias) f = __fadd_rn(f, bv);
     stg[j * 32 + lane] =
         OUT_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(f)) : __half_as_ushort(__float2half_rn(f));
   }
@@ -151,6 +160,7 @@ __device__ __forceinline__ void emit_row_any(const Params& p, int h, int n, int 
     return;
   }
   const float ws = n < p.N ? __ldg(p.w_scale + h * p.ws_sb + n) : 1.0f;
+  const float bv = (p.bias && n < p.N) ? load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n) : 0.0f;
   float as[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
@@ -158,9 +168,9 @@ __device__ __forceinline__ void emit_row_any(const Params& p, int h, int n, int 
     as[j] = m < p.M ? __ldg(p.a_scale + h * p.as_sb + m) : 1.0f;
   }
   if (p.out_dtype == CB_DTYPE_BF16)
-    emit_chunk_vec<1>(p, h, n - lane, lane, m0, t0, v, ws, as, stg);
+    emit_chunk_vec<1>(p, h, n - lane, lane, m0, t0, v, ws, bv, as, stg);
   else
-    emit_chunk_vec<0>(p, h, n - lane, lane, m0, t0, v, ws, as, stg);
+    emit_chunk_vec<0>(p, h, n - lane, lane, m0, t0, v, ws, bv, as, stg);
 }
 
 // Adds the published parts of contributors [c_lo, c_hi] (each its first
@@ -387,6 +397,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // aborted wait: work is skipped, but every named barrier is still reached
     // by all of them, so no thread can be left waiting on a barrier.
     pdl_wait_primary();
+    // Failure-detection test hook (cb_debug_force_wait_timeout): one thread
+    // waits, with a short limit, on a workspace word that nothing ever sets, so
+    // the wait expires and every role of the CTA takes its abort path.
+    if (p.dbg_wait_ns != 0 && threadIdx.x == 64)
+      wait_counter(p.status + 1, 1, abort_ptr, p.status, p.dbg_wait_ns);
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -411,6 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Scales of the rows this segment stores, loaded before any wait so the
       // stores after the last MMA depend on nothing in flight.
       float ws_pre = 1.0f;
+      float bias_pre = 0.0f;
       float as_pre[kPrefetch ? TN : 1];
       if constexpr (kPrefetch) {
         const bool stores = whole || collect;
@@ -418,11 +434,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < TN; ++j)
           as_pre[j] = (stores && !p.raw_f32 && m0 + j < p.M) ? __ldg(p.a_scale + h * p.as_sb + m0 + j) : 1.0f;
         if (stores && !p.raw_f32 && n < p.N) ws_pre = __ldg(p.w_scale + h * p.ws_sb + n);
+        if (stores && p.bias && n < p.N) bias_pre = load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n);
         // Consume the values here, so the compiler cannot sink the loads to
         // their use after the last MMA.
 #pragma unroll
         for (int j = 0; j < TN; ++j) asm volatile("" ::"f"(as_pre[j]));
         asm volatile("" ::"f"(ws_pre));
+        asm volatile("" ::"f"(bias_pre));
       }
       int32_t other[kPrefetch ? TN : 1];
       bool others_ready = true;
@@ -477,11 +495,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (p.vec_out) {
                 uint16_t* stg = epi_stage + (warp - 2) * 512;
                 if (p.out_dtype == CB_DTYPE_BF16)
-                  emit_chunk_vec<1>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, as16, stg);
+                  emit_chunk_vec<1>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
                 else
-                  emit_chunk_vec<0>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, as16, stg);
+                  emit_chunk_vec<0>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
               } else {
-                emit_row_pre(p, h, n, m0, c * 16, v, ws_pre, as16);
+                emit_row_pre(p, h, n, m0, c * 16, v, ws_pre, bias_pre, as16);
               }
             }
           } else {
@@ -544,11 +562,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (p.vec_out) {
                 uint16_t* stg = epi_stage + (warp - 2) * 512;
                 if (p.out_dtype == CB_DTYPE_BF16)
-                  emit_chunk_vec<1>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, as16, stg);
+                  emit_chunk_vec<1>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
                 else
-                  emit_chunk_vec<0>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, as16, stg);
+                  emit_chunk_vec<0>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
               } else {
-                emit_row_pre(p, h, n, m0, c * 16, v, ws_pre, as16);
+                emit_row_pre(p, h, n, m0, c * 16, v, ws_pre, bias_pre, as16);
               }
             }
           } else {
@@ -691,6 +709,10 @@ int launch_w8a8(const W8A8Launch& L, cudaStream_t stream) {
   p.out_sm = L.out_sm;
   p.acc_out = L.acc_out;
   p.raw_f32 = L.raw_f32;
+  p.bias = L.raw_f32 ? nullptr : L.bias;
+  p.bias_dtype = L.bias_dtype;
+  p.bias_sb = L.bias_sb;
+  p.dbg_wait_ns = debug_wait_ns();
   p.vec_out = (!L.raw_f32 && L.acc_out == nullptr &&
                (L.out_dtype == CB_DTYPE_BF16 || L.out_dtype == CB_DTYPE_F16) && L.N % 8 == 0 && aligned16(L.out) &&
                L.out_sm % 8 == 0 && (L.batch == 1 || L.out_sb % 8 == 0))

@@ -15,10 +15,16 @@
 //   - the first call on a device looks the array's device address up
 //     (cudaGetSymbolAddress, with that device current) and caches it; make that
 //     first call before any stream capture;
+//   - the cached address belongs to the device's CUDA context at the time of
+//     the first call: after a device reset (cudaDeviceReset, or a reset of the
+//     primary context) the library must be reloaded before calling it again;
 //   - every call on a device shares the one array and leaves its last contents
-//     there: the call clears the status word and counters on its stream before
+//     there: the call clears the arrival counters on its stream before
 //     launching, and two calls whose kernels overlap on the GPU (different
 //     streams, no ordering) race on the array;
+//   - the status word at the start of the array is not cleared by a call: a
+//     bounded device-side wait that expired in any call stays recorded until
+//     cb_w8a8_noalloc_status reads (and clears) it;
 //   - nothing here calls cudaMalloc, cudaFree or an allocating library routine.
 #include <cuda_runtime.h>
 
@@ -76,9 +82,11 @@ extern "C" int cb_w8a8_gemm_noalloc(const int8_t* aq, const float* a_scale, cons
   const int st = scratch_address(&scratch);
   if (st != CB_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // The status word and the arrival counters must start at zero; the partial
-  // slots are fully written before they are read.
-  if (cudaMemsetAsync(scratch, 0, kWsHeader + kWsCounters, s) != cudaSuccess) return CB_ERR_CUDA;
+  // The arrival counters must start at zero (a call that gave up a wait can
+  // leave some behind); the partial slots are fully written before they are
+  // read. The status word is left alone, so a timeout recorded by an earlier
+  // call survives until cb_w8a8_noalloc_status reads it.
+  if (cudaMemsetAsync(static_cast<char*>(scratch) + kWsHeader, 0, kWsCounters, s) != cudaSuccess) return CB_ERR_CUDA;
   W8A8Launch L = {};
   L.aq = aq;
   L.a_scale = a_scale;
@@ -102,4 +110,12 @@ extern "C" int cb_w8a8_gemm_noalloc(const int8_t* aq, const float* a_scale, cons
   L.workspace = scratch;
   L.workspace_bytes = kNoAllocScratchBytes;
   return launch_w8a8(L, s);
+}
+
+extern "C" int cb_w8a8_noalloc_status(int* device_status, cb_stream_t stream) {
+  using namespace cb;
+  void* scratch = nullptr;
+  const int st = scratch_address(&scratch);
+  if (st != CB_OK) return st;
+  return read_and_clear_status(scratch, device_status, reinterpret_cast<cudaStream_t>(stream));
 }

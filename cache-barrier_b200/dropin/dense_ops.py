@@ -9,7 +9,9 @@ call shapes for the int8 W8A8 and int4 W4A16 paths:
       a: int8 [M, K], K contiguous; b: int8 [K, N] column-major (b.t() is a
       contiguous [N, K] K-major weight); scale_a: fp32 per-token [M, 1] / [M] or
       per-tensor (one element); scale_b: fp32 per-channel [1, N] / [N] or
-      per-tensor. out = (a @ b)_int32 * scale_a * scale_b (+ bias), in out_dtype.
+      per-tensor. out = cvt((a @ b)_int32 * scale_a * scale_b (+ bias)): the
+      bias is added in fp32 before the one rounding to out_dtype, as vLLM's
+      epilogue does.
   scaled_int8_quant(x, scale=None) -> (q, scale [M, 1], None)
       dynamic per-token symmetric int8, rounding as the cache-barrier act-quant
       kernel (profiling/w8a8/w8a8_bmm.py:35-39: scale = max(amax/127, 1e-8),
@@ -66,11 +68,11 @@ def cutlass_scaled_mm(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor, s
     if out_dtype not in (torch.bfloat16, torch.float16):
         raise ValueError("out_dtype must be bfloat16 or float16")
     w_nk = b.t() if b.stride(0) == 1 else kmajor_int8_for(b)  # column-major b is K-major storage
-    out = ops.w8a8_gemm(a, w_nk, _per_row(scale_a, M, "scale_a"), _per_row(scale_b, N, "scale_b"),
-                        out_dtype=out_dtype)
-    if bias is not None:
-        out += bias.to(out_dtype)
-    return out
+    if bias is not None and (bias.numel() != N or bias.dtype not in (torch.bfloat16, torch.float16, torch.float32)):
+        raise ValueError(f"bias must have N={N} elements of a floating dtype")
+    # vLLM adds the bias in its fp32 epilogue, before the one rounding to out_dtype; so does the kernel
+    return ops.w8a8_gemm(a, w_nk, _per_row(scale_a, M, "scale_a"), _per_row(scale_b, N, "scale_b"),
+                         out_dtype=out_dtype, bias=None if bias is None else bias.reshape(N).contiguous())
 
 
 def scaled_int8_quant(x: torch.Tensor, scale: torch.Tensor | None = None, azp=None, symmetric: bool = True):

@@ -94,8 +94,21 @@ CB_API size_t cb_workspace_bytes(int op, int64_t batch, int64_t M, int64_t N, in
 
 /* Copies the workspace status word to *device_status after synchronizing the
    stream. Returns CB_ERR_DEVICE_TIMEOUT if a kernel recorded an expired wait
-   (and then clears the word), CB_OK otherwise. */
+   (and then clears the word and the workspace's arrival counters, which a
+   kernel that gave up a wait may leave behind), CB_OK otherwise. */
 CB_API int cb_workspace_status(void* workspace, int* device_status, cb_stream_t stream);
+
+/* Failure-detection test hook (no counterpart in the reference). With a
+   nonzero limit_ns, every later W8A8 GEMM launch (all W8A8 entry points and
+   the W4A4 path) makes one epilogue thread per CTA wait, bounded by limit_ns,
+   on a workspace word that nothing sets: the wait expires, the kernel records
+   CB_DEVERR_TIMEOUT in its status word and every role of the CTA takes its
+   abort path (skips its remaining work, drains its copies and MMAs, frees its
+   tensor memory), so the GPU context stays usable and the caller sees the
+   timeout through cb_workspace_status / cb_w8a8_noalloc_status. The output of
+   such a call is undefined. 0 (the default) turns the hook off. Process-wide;
+   for tests only. */
+CB_API void cb_debug_force_wait_timeout(uint64_t limit_ns);
 
 /* ---- activation quantization ------------------------------------------- */
 /* Per-(batch, row) symmetric int8: scale = max(amax/127, 1e-8),
@@ -124,6 +137,19 @@ CB_API int cb_w8a8_gemm(const int8_t* aq, const float* a_scale, const int8_t* w,
                  int out_dtype, int32_t* acc_out, int64_t batch, int64_t M, int64_t N, int64_t K,
                  const int64_t* strides, void* workspace, size_t workspace_bytes, cb_stream_t stream);
 
+/* cb_w8a8_gemm with an optional per-output-channel bias added in fp32 before
+   the output rounding:
+     out[b, m, n] = cvt( ((float)acc * a_scale[b, m]) * w_scale[b, n] + (float)bias[b * bias_stride_b + n] ).
+   This is where vLLM's cutlass_scaled_mm(a, b, scale_a, scale_b, out_dtype, bias)
+   adds its bias (in the fp32 epilogue), the call the reference's dense
+   harnesses make (profiling/dense_qwen/bench_l2_boundary.py:66-71,
+   profiling/dense_qwen/bench_dense_proj.py:113-115). bias: f16 / bf16 / f32,
+   NULL for none (then identical to cb_w8a8_gemm). */
+CB_API int cb_w8a8_gemm_bias(const int8_t* aq, const float* a_scale, const int8_t* w, const float* w_scale,
+                             const void* bias, int bias_dtype, int64_t bias_stride_b, void* out, int out_dtype,
+                             int32_t* acc_out, int64_t batch, int64_t M, int64_t N, int64_t K,
+                             const int64_t* strides, void* workspace, size_t workspace_bytes, cb_stream_t stream);
+
 /* Dynamic per-token activation quantization followed by the W8A8 GEMM, two
    launches chained with programmatic dependent launch so the GEMM's weight
    stream starts while the quantization runs. Replaces w8a8_bmm_full
@@ -145,10 +171,23 @@ CB_API int cb_w8a8_gemm_dynamic(const void* a, int a_dtype, int8_t* q_buf, float
    than 32 tokens) return CB_ERR_TOO_LARGE. The first call on a device looks the
    array up with that device current; make it before any stream capture. All
    calls on a device share the array: each clears its counters on its stream
-   first, and calls whose kernels overlap on the GPU race. */
+   first, and calls whose kernels overlap on the GPU race. The address lookup
+   is cached per device for the life of the process: after a device reset
+   (cudaDeviceReset or a primary-context reset) reload the library before
+   calling again. A bounded device-side wait that expires is recorded in the
+   array's status word, which calls do not clear: read it with
+   cb_w8a8_noalloc_status. */
 CB_API int cb_w8a8_gemm_noalloc(const int8_t* aq, const float* a_scale, const int8_t* w, const float* w_scale,
                                 void* out, int out_dtype, int32_t* acc_out, int64_t batch, int64_t M, int64_t N,
                                 int64_t K, const int64_t* strides, cb_stream_t stream);
+
+/* Status of cb_w8a8_gemm_noalloc calls on the current device (no counterpart
+   in the reference): synchronizes the stream, copies the scratch array's status
+   word to *device_status (nullable) and returns CB_ERR_DEVICE_TIMEOUT if any
+   call since the last read recorded an expired wait (then clears the word and
+   the array's counters), CB_OK otherwise. The device-side counterpart of
+   cb_workspace_status for callers that hold no workspace. */
+CB_API int cb_w8a8_noalloc_status(int* device_status, cb_stream_t stream);
 
 /* ---- W4A16 int4 group-dequant GEMM / batched INT4 BMM -------------------- */
 /* out[b, m, n] = sum_k a[b, m, k] * (q[b, k, n] * s[b, k / group_size, n]).

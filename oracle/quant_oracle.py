@@ -124,12 +124,18 @@ def gemm_i8_i32(aq: np.ndarray, wq_kn: np.ndarray) -> np.ndarray:
     return acc.astype(np.int32)
 
 
-def w8a8_epilogue(acc: np.ndarray, a_scale: np.ndarray, w_scale: np.ndarray, out_dtype: str) -> np.ndarray:
+def w8a8_epilogue(acc: np.ndarray, a_scale: np.ndarray, w_scale: np.ndarray, out_dtype: str,
+                  bias: np.ndarray | None = None) -> np.ndarray:
     """((float)acc * a_scale[m]) * w_scale[n], then cast (profiling/w8a8/w8a8_bmm.py:78-81).
-    acc [B, M, N] int32, a_scale [B, M] fp32, w_scale [B, N] fp32."""
+    acc [B, M, N] int32, a_scale [B, M] fp32, w_scale [B, N] fp32.
+    With ``bias`` ([B, N] or [N], values exactly representable in fp32) the bias
+    is added in fp32 before the cast, where vLLM's cutlass_scaled_mm adds it (the
+    call of profiling/dense_qwen/bench_l2_boundary.py:66-71)."""
     f = acc.astype(np.float32)
     f = (f * a_scale.astype(np.float32)[..., :, None]).astype(np.float32)
     f = (f * w_scale.astype(np.float32)[..., None, :]).astype(np.float32)
+    if bias is not None:
+        f = (f + np.asarray(bias, dtype=np.float32)[..., None, :]).astype(np.float32)
     return round_to(f, out_dtype)
 
 

@@ -34,7 +34,8 @@ def oracle_dtype(dtype: torch.dtype) -> str:
 
 
 def max_rel(got: np.ndarray, ref: np.ndarray) -> float:
-    """max |got - ref| / max |ref| (normwise maximum relative error)."""
+    """max |got - ref| / max |ref|: the norm-wise (infinity-norm) maximum relative
+    error. Looser than an element-wise bound; see elementwise_close."""
     denom = float(np.abs(ref).max())
     return float(np.abs(got - ref).max()) / (denom if denom > 0 else 1.0)
 
@@ -42,3 +43,24 @@ def max_rel(got: np.ndarray, ref: np.ndarray) -> float:
 def rel_l2(got: np.ndarray, ref: np.ndarray) -> float:
     denom = float(np.linalg.norm(ref))
     return float(np.linalg.norm(got - ref)) / (denom if denom > 0 else 1.0)
+
+
+def elementwise_close(got: np.ndarray, ref: np.ndarray, rtol: float, atol) -> bool:
+    """Element-wise relative error bound with an absolute term:
+    |got - ref| <= rtol * |ref| + atol for every element (atol a scalar or an
+    array shaped like ref).
+
+    A pure element-wise relative error is undefined for outputs that cancel to
+    near zero; the W4A16 tests pass atol = u * (|a| @ |w|), the rigorous bound on
+    what rounding the dequantized weight operand to the activation dtype (unit
+    roundoff u: 2^-8 for bf16, 2^-11 for f16) can change in each output."""
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    return bool(np.all(np.abs(got - ref) <= rtol * np.abs(ref) + atol))
+
+
+def operand_rounding_bound(a_f32: np.ndarray, w_f32: np.ndarray, dtype) -> np.ndarray:
+    """u * (|a| @ |w|): the largest change that rounding each weight operand
+    element w to `dtype` (relative error <= u) can make to each output of a @ w."""
+    u = 2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11
+    return u * np.matmul(np.abs(np.asarray(a_f32, np.float64)), np.abs(np.asarray(w_f32, np.float64)))
