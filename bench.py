@@ -19,10 +19,16 @@ Reported (one JSON line from rank 0):
              pinned host activations copied in and outputs copied out every GEMM
   roofline   the GEMM kernel alone: algorithmic bytes per launch / CUDA-event time
   cpu_baseline  the oracle's restatement of the reference's CPU path (rank 0, N = 1)
-plus the cuBLAS bf16 comparison (dequantized weights, same rotation), and W4A16
-group-128 and NVFP4 (block-scaled FP4 tensor cores) measurements of the same shape.
+plus the cuBLAS bf16 comparison (dequantized weights, same rotation), W4A16
+group-128 and NVFP4 (block-scaled FP4 tensor cores) measurements of the same shape,
+and (the ``tp`` object) the tensor-parallel decode step of a 64-layer dense
+decoder's projections at tp = N: us per layer for W8A8, W4A16 and bf16, the
+all-reduce's share (NCCL and the one-shot NVLink all-reduce), weight GB/s per
+GPU, and the per-GPU projection shards on either side of the capacity gate.
+The headline ``value`` stays the per-GPU W8A8 workload at every N (replicas),
+so the metric is the same for every N.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--tp on|off]
 """
 
 from __future__ import annotations
@@ -48,6 +54,8 @@ COPIES = 4
 CYCLES = 32  # passes over TOKENS per step
 W4_COPIES = 8
 GROUP = 128
+TP_TOKENS = (1, 8, 32, 64)
+TP_PRECISIONS = ("w8a8", "w4a16", "bf16")
 
 
 def parse_args():
@@ -56,6 +64,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="cb200", choices=["cb200", "reference"])
+    ap.add_argument("--tp", default="on", choices=["on", "off"],
+                    help="also time the tensor-parallel dense decode step at tp = N (the 'tp' object)")
     return ap.parse_args()
 
 
@@ -453,6 +463,33 @@ def main():
     except Exception as e:  # noqa: BLE001
         fp4 = {"error": repr(e)}
 
+    # ---------------- tensor-parallel dense decode at tp = N ----------------
+    # 64-layer 27B-class decoder projections (QKV and gate-up column-parallel, O
+    # and down row-parallel, each followed by an all-reduce of [T, 5120] bf16),
+    # one CUDA graph per decode step, max over ranks; NCCL and the one-shot
+    # NVLink all-reduce both measured at N > 1.
+    tp = None
+    if args.tp == "on":
+        try:
+            sys.path.insert(0, os.path.join(ROOT, "cache-barrier_b200", "harness"))
+            import dense_tp
+
+            del g_dyn, g_mm
+            g_dyn = g_mm = None
+            torch.cuda.empty_cache()
+            logf = (lambda m: print(m, file=sys.stderr, flush=True)) if rank == 0 else (lambda m: None)
+            _rows, _prows, summary = dense_tp.measure(world, rank, dev, TP_TOKENS, TP_PRECISIONS,
+                                                      ["nccl", "peer"], steps=10, warmup=3, log=logf)
+            tp = {"workload": "dense 27B-class decoder projections, 64 layers, hidden 5120, 40 q + 8 kv heads of "
+                              "128, FFN 17408; QKV/gate-up column-parallel, O/down row-parallel + all-reduce; "
+                              "W8A8 per-channel int8, W4A16 g128 int4, bf16 cuBLAS; random N(0, 0.02) weights",
+                  "timing": "one CUDA graph per decode step, 10 replays after 3 warm-up, max over ranks; "
+                            "per-projection: a graph of one projection's GEMM in all 64 layers",
+                  **summary}
+            assert ops.device_status(dev) == 0
+        except Exception as e:  # noqa: BLE001
+            tp = {"error": repr(e)}
+
     # ---------------- CPU baseline (rank 0, N = 1) ----------------
     cpu = None
     if world == 1 and rank == 0:
@@ -490,7 +527,7 @@ def main():
                 "step": f"{CYCLES} passes over T=1,8,16,32 = {gemms_per_step} GEMMs (act-quant + GEMM launches), "
                         "one CUDA graph replay",
                 "l2": f"inputs larger than L2: weights rotate over {COPIES} copies = 256 MiB per GEMM cycle",
-                "parallelism": f"replicas x{world}",
+                "parallelism": f"replicas x{world} (headline); tensor parallel tp={world} (the tp object)",
             },
             "us_per_gemm_per_gpu": round(us_per_gemm_gpu, 3),
             "per_token_kernel_us": {str(T): round(v, 3) for T, v in per_t.items()},
@@ -513,6 +550,7 @@ def main():
             "clocks": clock_info,
             "w4a16": w4,
             "nvfp4": fp4,
+            "tp": tp,
         }
         print(json.dumps(line), flush=True)
 

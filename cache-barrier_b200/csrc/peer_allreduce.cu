@@ -2,22 +2,25 @@
 // row-parallel projections (a [T, hidden] bf16/f16 tensor per rank, tens to
 // hundreds of KiB), where a library ring all-reduce is latency-bound.
 //
-// Each rank owns a symmetric area (allocated once by cb_symm_alloc, mapped into
-// every peer's address space through CUDA IPC handles exchanged by the host):
-//   data  [2 parities][world][slot_elems]   16-bit partials written by the ranks
-//   flags [2 parities][world][kMaxCtas]     epoch stamps, one per (rank, CTA)
-//   epoch [kMaxCtas]                        this rank's per-CTA call counters
-// A call runs the same grid on every rank. CTA b of rank r takes chunk b of the
-// tensor: it stores the chunk into slot r of every rank's data area (plain
-// stores, local or peer), fences at system scope, then stamps flags[p][r][b] =
-// epoch on every rank with a release store. It waits (bounded) until all world
-// stamps for chunk b in its own flags read the epoch, sums the world slots in
-// rank order in fp32 and writes the rounded result, so every rank produces the
-// same values. The two parities double-buffer consecutive calls: a rank writes
-// parity p of call e+1 only after it saw every peer's stamp of call e, and a
-// peer stamps call e only after it finished reading call e-1 (same parity as
-// e+1) in the same CTA. The per-CTA counters advance on the device, so the
-// call sequence works inside CUDA graphs.
+// Low-latency protocol: every 8-byte word a rank sends carries two 16-bit
+// values and the 32-bit number of the call, written with one 64-bit store
+// (single-copy atomic), so a reader that sees the call number in a word has
+// its data too: no fences and no separate flags. Each rank owns a symmetric
+// area (allocated once by cb_symm_alloc, mapped into every peer's address space
+// through CUDA IPC handles exchanged by the host):
+//   recv  [2 parities][world][slot_pairs] 64-bit words (data | call << 32)
+//   ctl   [call number of the last completed call, CTA finish counter]
+// A call runs the same grid on every rank; CTA b takes pairs [p0, p1) of the
+// tensor. It stores its pairs into slot `rank` of every rank's recv area (plain
+// 64-bit stores, local or peer), then polls its own recv area (bounded) until
+// every rank's word for each of its pairs carries this call's number, sums the
+// world values in rank order in fp32 and writes the rounded result, so every
+// rank produces the same values. The call number is read from ctl after
+// griddepcontrol.wait and advanced by the last CTA to finish, so calls work
+// inside CUDA graphs. The two parities keep a fast rank's next-but-one call
+// from overwriting words a slow rank still reads: a rank starts call e + 2 only
+// after finishing call e + 1, which needed every peer's call-(e + 1) words,
+// which each peer sent only after finishing call e.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -32,34 +35,35 @@ namespace cb {
 namespace {
 
 constexpr int kMaxWorld = 8;
-constexpr int kMaxCtas = 64;
+constexpr int kMaxCtas = 128;
 constexpr int kThreads = 256;
+constexpr long long kPairsPerCta = 512;
 
 struct PeerArgs {
   const uint16_t* in;
   uint16_t* out;
-  long long n;
-  long long slot_elems;
+  long long n;           // elements
+  long long slot_pairs;  // words per (parity, rank) slot
   int dtype;
   int rank, world;
-  uint16_t* data[kMaxWorld];  // every rank's data area, as mapped in this process
-  int* flags[kMaxWorld];      // every rank's flag area
-  int* epoch;                 // this rank's per-CTA counters
-  int* status;                // this rank's status word (bit CB_DEVERR_TIMEOUT on a wait that ran out)
+  unsigned long long* recv[kMaxWorld];  // every rank's recv area, as mapped in this process
+  unsigned int* ctl;                    // this rank's [last call, finish counter]
+  int* status;                          // this rank's status word (bit CB_DEVERR_TIMEOUT on a wait that ran out)
 };
 
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
-__device__ __forceinline__ float to_f(uint16_t v, int dtype) {
-  if (dtype == CB_DTYPE_BF16) return __bfloat162float(__ushort_as_bfloat16(v));
-  return __half2float(__ushort_as_half(v));
+__device__ __forceinline__ float to_f(uint32_t v, int dtype) {
+  const uint16_t h = static_cast<uint16_t>(v);
+  if (dtype == CB_DTYPE_BF16) return __bfloat162float(__ushort_as_bfloat16(h));
+  return __half2float(__ushort_as_half(h));
 }
 __device__ __forceinline__ uint16_t from_f(float v, int dtype) {
   if (dtype == CB_DTYPE_BF16) return __bfloat16_as_ushort(__float2bfloat16_rn(v));
@@ -69,82 +73,71 @@ __device__ __forceinline__ uint16_t from_f(float v, int dtype) {
 __global__ void __launch_bounds__(kThreads) peer_allreduce_kernel(const PeerArgs a) {
   pdl_launch_dependents();
   pdl_wait_primary();  // the partial comes from the preceding kernel
-  __shared__ int sh_epoch;
-  __shared__ int sh_ok;
-  const int b = blockIdx.x;
+  __shared__ unsigned int sh_call;
+  __shared__ int sh_abort;
   if (threadIdx.x == 0) {
-    sh_epoch = ++a.epoch[b];
-    sh_ok = 1;
+    sh_call = *reinterpret_cast<volatile unsigned int*>(a.ctl) + 1u;
+    sh_abort = 0;
   }
   __syncthreads();
-  const int e = sh_epoch;
-  const int par = e & 1;
-  const long long c0 = static_cast<long long>(b) * a.n / gridDim.x;
-  const long long c1 = static_cast<long long>(b + 1) * a.n / gridDim.x;
-  const long long slot = static_cast<long long>(par) * a.world * a.slot_elems + static_cast<long long>(a.rank) * a.slot_elems;
+  const unsigned int call = sh_call;
+  const unsigned long long tag = static_cast<unsigned long long>(call) << 32;
+  const int par = static_cast<int>(call & 1u);
+  const long long pairs = (a.n + 1) / 2;
+  const long long p0 = static_cast<long long>(blockIdx.x) * pairs / gridDim.x;
+  const long long p1 = static_cast<long long>(blockIdx.x + 1) * pairs / gridDim.x;
+  const long long my_slot = (static_cast<long long>(par) * a.world + a.rank) * a.slot_pairs;
 
-  // 1. push this rank's chunk into slot `rank` of every rank: 16-byte stores
-  //    (one NVLink write carries 8 values; 2-byte stores would each be a packet)
-  const long long v0 = (c0 + 7) / 8, v1 = c1 / 8;  // whole 8-element vectors inside the chunk
-  for (long long j = v0 + threadIdx.x; j < v1; j += blockDim.x) {
-    const uint4 v = reinterpret_cast<const uint4*>(a.in)[j];
-    for (int r = 0; r < a.world; ++r) reinterpret_cast<uint4*>(a.data[r] + slot)[j] = v;
+  // 1. push: this rank's pairs into slot `rank` of every rank (8-byte words)
+  for (long long i = p0 + threadIdx.x; i < p1; i += blockDim.x) {
+    const uint32_t lo = a.in[2 * i];
+    const uint32_t hi = (2 * i + 1 < a.n) ? a.in[2 * i + 1] : 0u;
+    const unsigned long long w = tag | (hi << 16) | lo;
+    for (int r = 0; r < a.world; ++r) st_relaxed_sys_u64(a.recv[r] + my_slot + i, w);
   }
-  for (long long i = c0 + threadIdx.x; i < c1; i += blockDim.x) {  // ragged ends
-    if (i >= v0 * 8 && i < v1 * 8) continue;
-    const uint16_t v = a.in[i];
-    for (int r = 0; r < a.world; ++r) a.data[r][slot + i] = v;
+  // 2. pull: wait (bounded) for every rank's word of each pair, sum in rank order
+  const unsigned long long* mine = a.recv[a.rank] + static_cast<long long>(par) * a.world * a.slot_pairs;
+  const unsigned long long t0 = global_timer_ns();
+  for (long long i = p0 + threadIdx.x; i < p1; i += blockDim.x) {
+    float acc0 = 0.0f, acc1 = 0.0f;
+    for (int r = 0; r < a.world; ++r) {
+      const unsigned long long* src = mine + static_cast<long long>(r) * a.slot_pairs + i;
+      unsigned long long w = ld_relaxed_sys_u64(src);
+      int spins = 0;
+      while ((w >> 32) != call) {
+        if ((++spins & 63) == 0) {
+          if (*reinterpret_cast<volatile int*>(&sh_abort)) break;
+          if (global_timer_ns() - t0 > kWaitLimitNs) {
+            sh_abort = 1;
+            atomicOr(a.status, CB_DEVERR_TIMEOUT);
+            break;
+          }
+        }
+        w = ld_relaxed_sys_u64(src);
+      }
+      acc0 += to_f(static_cast<uint32_t>(w), a.dtype);
+      acc1 += to_f(static_cast<uint32_t>(w >> 16), a.dtype);
+    }
+    a.out[2 * i] = from_f(acc0, a.dtype);
+    if (2 * i + 1 < a.n) a.out[2 * i + 1] = from_f(acc1, a.dtype);
   }
+  // 3. the last CTA to finish records this call as completed
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int r = 0; r < a.world; ++r)
-      st_release_sys(a.flags[r] + (par * kMaxWorld + a.rank) * kMaxCtas + b, e);
-  }
-  // 2. wait for every rank's stamp of this chunk (bounded)
-  if (threadIdx.x < a.world) {
-    const int* f = a.flags[a.rank] + (par * kMaxWorld + threadIdx.x) * kMaxCtas + b;
-    const unsigned long long t0 = global_timer_ns();
-    while (ld_acquire_sys(f) != e) {
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        sh_ok = 0;
-        atomicOr(a.status, CB_DEVERR_TIMEOUT);
-        break;
-      }
+    __threadfence();
+    if (atomicAdd(&a.ctl[1], 1u) == gridDim.x - 1) {
+      a.ctl[1] = 0;
+      a.ctl[0] = call;
+      __threadfence();
     }
-  }
-  __syncthreads();
-  if (!sh_ok) return;
-  // 3. sum the world slots in rank order
-  const uint16_t* mine = a.data[a.rank] + static_cast<long long>(par) * a.world * a.slot_elems;
-  for (long long j = v0 + threadIdx.x; j < v1; j += blockDim.x) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int r = 0; r < a.world; ++r) {
-      const uint4 v = reinterpret_cast<const uint4*>(mine + static_cast<long long>(r) * a.slot_elems)[j];
-      const uint16_t* h = reinterpret_cast<const uint16_t*>(&v);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] += to_f(h[q], a.dtype);
-    }
-    uint4 o;
-    uint16_t* oh = reinterpret_cast<uint16_t*>(&o);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) oh[q] = from_f(acc[q], a.dtype);
-    reinterpret_cast<uint4*>(a.out)[j] = o;
-  }
-  for (long long i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
-    if (i >= v0 * 8 && i < v1 * 8) continue;
-    float acc = 0.0f;
-    for (int r = 0; r < a.world; ++r) acc += to_f(mine[static_cast<long long>(r) * a.slot_elems + i], a.dtype);
-    a.out[i] = from_f(acc, a.dtype);
   }
 }
 
 }  // namespace
 
 size_t symm_bytes(int world, int64_t slot_elems) {
-  const size_t data = 2ull * world * static_cast<size_t>(slot_elems) * 2;
-  const size_t flags = 2ull * kMaxWorld * kMaxCtas * sizeof(int);
-  return align_up(data, 256) + flags + kMaxCtas * sizeof(int) + 256;
+  const size_t recv = 2ull * world * static_cast<size_t>((slot_elems + 1) / 2) * 8;
+  return align_up(recv, 256) + 256;  // + ctl
 }
 
 }  // namespace cb
@@ -204,28 +197,26 @@ CB_API int cb_peer_allreduce(const void* in, void* out, int64_t elems, int dtype
   if (elems > slot_elems) return CB_ERR_TOO_LARGE;
   if (elems == 0) return CB_OK;
   if (!in || !out || !symm_areas || !status) return CB_ERR_INVALID_ARG;
-  // 16-byte vector paths: in, out and every slot start on a 16-byte boundary
-  if (!aligned16(in) || !aligned16(out) || slot_elems % 8 != 0) return CB_ERR_ALIGNMENT;
+  // 16-bit elements
+  if ((reinterpret_cast<uintptr_t>(in) & 1u) || (reinterpret_cast<uintptr_t>(out) & 1u)) return CB_ERR_ALIGNMENT;
   PeerArgs a = {};
   a.in = static_cast<const uint16_t*>(in);
   a.out = static_cast<uint16_t*>(out);
   a.n = elems;
-  a.slot_elems = slot_elems;
+  a.slot_pairs = (slot_elems + 1) / 2;
   a.dtype = dtype;
   a.rank = rank;
   a.world = world;
-  const size_t data_bytes = align_up(2ull * world * static_cast<size_t>(slot_elems) * 2, 256);
+  const size_t recv_bytes = align_up(2ull * world * static_cast<size_t>(a.slot_pairs) * 8, 256);
   for (int r = 0; r < world; ++r) {
     if (!symm_areas[r]) return CB_ERR_INVALID_ARG;
-    char* base = static_cast<char*>(symm_areas[r]);
-    a.data[r] = reinterpret_cast<uint16_t*>(base);
-    a.flags[r] = reinterpret_cast<int*>(base + data_bytes);
+    a.recv[r] = static_cast<unsigned long long*>(symm_areas[r]);
   }
-  a.epoch = reinterpret_cast<int*>(static_cast<char*>(symm_areas[rank]) + data_bytes + 2ull * kMaxWorld * kMaxCtas * sizeof(int));
+  a.ctl = reinterpret_cast<unsigned int*>(static_cast<char*>(symm_areas[rank]) + recv_bytes);
   a.status = status;
-  // one CTA per ~4K elements, at most kMaxCtas; the grid depends only on elems,
-  // so every rank runs the same grid for the same call
-  long long ctas = (elems + 4095) / 4096;
+  // one CTA per kPairsPerCta pairs, at most kMaxCtas; the grid depends only on
+  // elems, so every rank runs the same grid for the same call
+  long long ctas = ((elems + 1) / 2 + kPairsPerCta - 1) / kPairsPerCta;
   if (ctas > kMaxCtas) ctas = kMaxCtas;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(ctas));

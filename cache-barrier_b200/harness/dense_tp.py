@@ -21,7 +21,7 @@ generated per shard from a seed of (layer, projection, rank); 64 distinct
 layers keep the per-GPU working set far above L2.
 
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 cache-barrier_b200/harness/dense_tp.py \\
-        --tokens 1,8,32,64 --precisions w8a8,w4a16,bf16 --out dense_tp_tp8.json
+        --tokens 1,8,32,64 --precisions w8a8,w4a16,bf16 --allreduce nccl,peer --out dense_tp_tp8.json
 
 The projection backend is injectable (``Backend``) so the sharding and
 reduction logic runs on CPU with gloo ranks and an fp32 matmul in the tests.
@@ -222,6 +222,14 @@ class TPStack:
         for i in range(self.d.layers):
             self.layer(i, reduce)
 
+    def proj_step(self, proj: str):
+        """One projection's GEMM in every layer (no all-reduce): per-GEMM timing of one shard shape."""
+        b, sc = self.backend, self.scratch
+        x, out = {"qkv": (self.x, self.qkv_out), "o": (self.o_in, self.o_out), "gate_up": (self.x, self.gu_out),
+                  "down": (self.act_in, self.d_out)}[proj]
+        for i in range(self.d.layers):
+            b.run(x, self.handles[i][proj], out, sc)
+
     def weight_bytes(self) -> int:
         return self.d.layers * sum(self.backend.weight_bytes(*shard_shape(self.d, p, self.tp)) for p in PROJS)
 
@@ -256,6 +264,108 @@ def _max_over_ranks(v: float, device) -> float:
     return float(t.item())
 
 
+def measure(world: int, rank: int, dev, tokens, precisions, modes, steps: int = 10, warmup: int = 3,
+            layers: int = 64, per_projection: bool = True, log=print):
+    """Times the decode step of the tensor-parallel stack at tp = world on this rank (every rank calls it
+    with the same arguments). Returns the rows (max over ranks of CUDA-event time) and a summary."""
+    from common import ClockSampler
+
+    d = Dims(layers=layers)
+    peer = None
+    if world > 1 and "peer" in modes:
+        sys.path.insert(0, os.path.dirname(HERE))
+        from cb200.peer import PeerAllReduce
+
+        peer = PeerAllReduce(max(tokens) * d.hidden, device=dev)
+    if world == 1:
+        modes = ["none"]
+    rows, proj_rows = [], []
+    for prec in precisions:
+        backend = BACKENDS[prec]()
+        stack = TPStack(d, world, rank, backend, dev, seed=1234)
+        for T in tokens:
+            stack.bind(T)
+            ms_noar = None
+            for mode in modes:
+                stack.allreduce = peer if mode == "peer" else None
+                if world > 1:
+                    dist.barrier()
+                with ClockSampler(dev.index) as clk:
+                    ms = _max_over_ranks(_time_graph(lambda: stack.step(world > 1), steps, warmup), dev)
+                    if ms_noar is None:
+                        ms_noar = _max_over_ranks(_time_graph(lambda: stack.step(False), steps, warmup), dev)
+                wb = stack.weight_bytes()
+                row = {"precision": prec, "tokens": T, "tp": world, "layers": d.layers, "allreduce": mode,
+                       "step_ms": round(ms, 4), "us_per_layer": round(ms * 1e3 / d.layers, 3),
+                       "step_ms_without_allreduce": round(ms_noar, 4),
+                       "allreduce_us_per_layer": round((ms - ms_noar) * 1e3 / d.layers, 3),
+                       "tokens_per_s": round(T / (ms * 1e-3), 1),
+                       "weight_bytes_per_gpu": wb,
+                       "weight_gbs_per_gpu": round(wb / (ms_noar * 1e-3) / 1e9, 1),
+                       "clocks": clk.info}
+                rows.append(row)
+                log(f"tp={world} {prec:6s} T={T:3d} [{mode}]: {row['us_per_layer']:9.2f} us/layer "
+                    f"(all-reduce {row['allreduce_us_per_layer']:.2f}), {row['weight_gbs_per_gpu']} GB/s/GPU")
+            if per_projection:
+                for proj in PROJS:
+                    N, K = shard_shape(d, proj, world)
+                    ms = _max_over_ranks(_time_graph(lambda: stack.proj_step(proj), steps, warmup), dev)
+                    proj_rows.append({"precision": prec, "tokens": T, "tp": world, "proj": proj, "N": N, "K": K,
+                                      "bf16_shard_mb": round(2 * N * K / 1e6, 2),
+                                      "us_per_gemm": round(ms * 1e3 / d.layers, 3)})
+        del stack
+        torch.cuda.empty_cache()
+    if peer is not None:
+        assert int(peer.status.item()) == 0, "peer all-reduce reported a timeout"
+        peer.close()
+    return rows, proj_rows, summarize(rows, proj_rows, world)
+
+
+def summarize(rows, proj_rows, world: int) -> dict:
+    """Per token count: the best exchange per precision, the all-reduce share, quantized vs bf16, and the
+    gate at this tp: the per-GPU projection shards (bf16-equivalent MB) where each quantized kernel wins."""
+    out = {"tp": world, "per_tokens": {}}
+    tokens = sorted({r["tokens"] for r in rows})
+    for T in tokens:
+        best = {}
+        for r in rows:
+            if r["tokens"] != T:
+                continue
+            cur = best.get(r["precision"])
+            if cur is None or r["us_per_layer"] < cur["us_per_layer"]:
+                best[r["precision"]] = r
+        ent = {}
+        for prec, r in best.items():
+            e = {"us_per_layer": r["us_per_layer"], "allreduce": r["allreduce"],
+                 "allreduce_us_per_layer": r["allreduce_us_per_layer"],
+                 "allreduce_share": round(r["allreduce_us_per_layer"] / r["us_per_layer"], 3) if world > 1 else 0.0,
+                 "weight_gbs_per_gpu": r["weight_gbs_per_gpu"]}
+            modes = {x["allreduce"]: x["allreduce_us_per_layer"] for x in rows
+                     if x["tokens"] == T and x["precision"] == prec}
+            if len(modes) > 1:
+                e["allreduce_us_per_layer_by_exchange"] = modes
+            if "bf16" in best and prec != "bf16":
+                e["speedup_vs_bf16"] = round(best["bf16"]["us_per_layer"] / r["us_per_layer"], 3)
+            ent[prec] = e
+        gate = {}
+        bf = {p["proj"]: p for p in proj_rows if p["tokens"] == T and p["precision"] == "bf16"}
+        for prec in {p["precision"] for p in proj_rows} - {"bf16"}:
+            shards = []
+            for p in proj_rows:
+                if p["tokens"] == T and p["precision"] == prec and p["proj"] in bf:
+                    shards.append({"proj": p["proj"], "bf16_shard_mb": p["bf16_shard_mb"], "us": p["us_per_gemm"],
+                                   "bf16_us": bf[p["proj"]]["us_per_gemm"],
+                                   "speedup": round(bf[p["proj"]]["us_per_gemm"] / p["us_per_gemm"], 3)})
+            shards.sort(key=lambda x: x["bf16_shard_mb"])
+            wins = [x["bf16_shard_mb"] for x in shards if x["speedup"] > 1.0]
+            loses = [x["bf16_shard_mb"] for x in shards if x["speedup"] <= 1.0]
+            gate[prec] = {"shards": shards,
+                          "smallest_winning_shard_mb": min(wins) if wins else None,
+                          "largest_losing_shard_mb": max(loses) if loses else None}
+        out["per_tokens"][str(T)] = {"layer": ent, "gate": gate}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", default="1,8,32,64")
@@ -263,7 +373,8 @@ def main():
     ap.add_argument("--layers", type=int, default=64)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--allreduce", default="nccl", help="comma-separated: nccl, peer (NVLink one-shot kernel)")
+    ap.add_argument("--allreduce", default="nccl,peer", help="comma-separated: nccl, peer (NVLink one-shot kernel)")
+    ap.add_argument("--no-per-projection", action="store_true")
     ap.add_argument("--out", default=None)
     args = ap.parse_args()
 
@@ -274,55 +385,21 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    from common import ClockSampler, gpu_info, save_json
+    from common import gpu_info, save_json
 
-    d = Dims(layers=args.layers)
-    tokens = [int(t) for t in args.tokens.split(",")]
-    modes = args.allreduce.split(",") if world > 1 else ["none"]
-    peer = None
-    if "peer" in modes:
-        sys.path.insert(0, os.path.dirname(HERE))
-        from cb200.peer import PeerAllReduce
-
-        peer = PeerAllReduce(max(tokens) * d.hidden, device=dev)
-    rows = []
-    for prec in args.precisions.split(","):
-        backend = BACKENDS[prec]()
-        stack = TPStack(d, world, rank, backend, dev, seed=1234)
-        for T, mode in [(T, m) for T in tokens for m in modes]:
-            stack.bind(T)
-            stack.allreduce = peer if mode == "peer" else None
-            if world > 1:
-                dist.barrier()
-            with ClockSampler(local) as clk:
-                ms = _max_over_ranks(_time_graph(lambda: stack.step(True), args.steps, args.warmup), dev)
-                ms_noar = _max_over_ranks(_time_graph(lambda: stack.step(False), args.steps, args.warmup), dev)
-            wb = stack.weight_bytes()
-            row = {"precision": prec, "tokens": T, "tp": world, "layers": d.layers, "allreduce": mode,
-                   "step_ms": round(ms, 4), "us_per_layer": round(ms * 1e3 / d.layers, 3),
-                   "step_ms_without_allreduce": round(ms_noar, 4),
-                   "allreduce_us_per_layer": round((ms - ms_noar) * 1e3 / d.layers, 3),
-                   "tokens_per_s": round(T / (ms * 1e-3), 1),
-                   "weight_bytes_per_gpu": wb,
-                   "weight_gbs_per_gpu": round(wb / (ms_noar * 1e-3) / 1e9, 1),
-                   "clocks": clk.info}
-            rows.append(row)
-            if rank == 0:
-                print(f"tp={world} {prec:6s} T={T:3d} [{mode}]: {row['us_per_layer']:9.2f} us/layer "
-                      f"(all-reduce {row['allreduce_us_per_layer']:.2f}), {row['weight_gbs_per_gpu']} GB/s/GPU",
-                      flush=True)
-        del stack
-        torch.cuda.empty_cache()
+    rows, proj_rows, summary = measure(world, rank, dev, [int(t) for t in args.tokens.split(",")],
+                                       args.precisions.split(","), args.allreduce.split(","), args.steps,
+                                       args.warmup, args.layers, not args.no_per_projection,
+                                       log=(lambda m: print(m, flush=True)) if rank == 0 else (lambda m: None))
     if rank == 0:
-        out = {"experiment": "dense_tp_projections", "dims": d.__dict__, "tp": world, "gpu": gpu_info(),
-               "method": "one CUDA graph per decode step (64 layers x 4 projections + 2 NCCL all-reduces per "
-                         "layer); max over ranks of CUDA-event time; weights rotate naturally across layers",
-               "rows": rows}
+        out = {"experiment": "dense_tp_projections", "dims": Dims(layers=args.layers).__dict__, "tp": world,
+               "gpu": gpu_info(),
+               "method": "one CUDA graph per decode step (64 layers x 4 projections + 2 all-reduces per layer); "
+                         "max over ranks of CUDA-event time; weights rotate naturally across layers; "
+                         "per-projection rows: a graph of one projection's GEMM in all 64 layers",
+               "rows": rows, "projections": proj_rows, "summary": summary}
         if args.out:
             save_json(args.out, out)
-    if peer is not None:
-        assert int(peer.status.item()) == 0, "peer all-reduce reported a timeout"
-        peer.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

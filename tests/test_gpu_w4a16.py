@@ -124,6 +124,47 @@ def test_w4a16_launcher_call_shape(cuda_device, golden):
     assert max_rel(c.float().cpu().numpy(), d["c_simple"].astype(np.float32)) <= 2e-3
 
 
+# Decode shapes with activations of very different magnitude per token and per
+# 128-k block, all-zero tokens and blocks, and a K that is not a multiple of 128.
+@pytest.mark.parametrize("B,M,N,K,act_dtype", [
+    (1, 7, 384, 200, torch.bfloat16),
+    (3, 24, 640, 1152, torch.float16),
+    (1, 9, 4096, 4096, torch.bfloat16),
+    (2, 32, 256, 8192, torch.float16),
+])
+def test_w4a16_decode_dynamic_range(cuda_device, B, M, N, K, act_dtype):
+    from cb200 import _lib as L
+    from cb200 import ops
+    a, q, s = _int4_problem(B, M, N, K, 128, seed=B + M + N + K, act_dtype=act_dtype, scale_dtype=act_dtype)
+    af = a.float()
+    af[:, 0, :] *= 1e3 if act_dtype == torch.bfloat16 else 50.0  # a large token
+    af[:, -1, :] *= 1e-3  # a small token
+    if M > 2:
+        af[:, 1, :] = 0.0  # an all-zero token
+    af[:, :, 128:256] *= 0.0 if K > 256 else 1.0  # an all-zero k-block for every token
+    if K >= 512:
+        af[:, :, 384:512] *= 64.0  # one k-block much larger than the rest of its row
+    a = af.to(act_dtype)
+    ref = O.w4a16_gemm(to_np_f32(a), q.numpy(), to_np_f32(s), 128)
+    packed = torch.from_numpy(O.pack_i32_k8n(q.numpy())).to(cuda_device)
+    native = ops.repack_w4(packed, L.CB_W4_I32_K8N, K, N)
+    out = ops.w4a16_gemm(a.to(cuda_device), native, s.to(cuda_device), N, 128, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    bound = operand_rounding_bound(to_np_f32(a), O.dequant_w4(q.numpy(), to_np_f32(s), 128), act_dtype)
+    assert elementwise_close(got, ref, 1e-2, bound)
+    # per token row (rows differ by up to 10^6 in magnitude): the 1e-2 bound
+    # norm-wise within each row, not just against the largest row
+    for b in range(B):
+        for m in range(M):
+            r = ref[b, m]
+            if np.abs(r).max() > 0:
+                assert max_rel(got[b, m], r) <= 1e-2, (b, m)
+            else:
+                assert np.all(got[b, m] == 0.0), (b, m)
+    assert ops.device_status(cuda_device) == 0
+
+
 def test_w4a16_strided_output_and_canary(cuda_device):
     from cb200 import _lib as L
     from cb200 import ops
