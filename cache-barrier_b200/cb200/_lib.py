@@ -39,6 +39,11 @@ CB_OP_W4A16 = 1
 CB_OP_W4A4 = 2
 CB_OP_NVFP4 = 3
 
+# fp8 activation quantization modes
+CB_FP8_PER_TOKEN = 0
+CB_FP8_PER_TENSOR_DYNAMIC = 1
+CB_FP8_STATIC = 2
+
 # W4A4 nibble modes
 CB_W4A4_SIGNED = 0
 CB_W4A4_REF_UINT8_WRAP = 1
@@ -64,6 +69,9 @@ SIGNATURES = {
     "cb_w8a8_gemm": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _sz, _vp]),
     "cb_w8a8_gemm_bias": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _i64, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp,
                                  _vp, _sz, _vp]),
+    "cb_quant_act_fp8": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _int, _vp]),
+    "cb_fp8_gemm": (_int, [_vp, _vp, _int, _vp, _vp, _int, _vp, _int, _vp, _int, _i64, _i64, _i64, _i64, _vp, _vp, _sz,
+                           _vp]),
     "cb_w8a8_gemm_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "cb_w8a8_noalloc_status": (_int, [ctypes.POINTER(_int), _vp]),
     "cb_debug_force_wait_timeout": (None, [ctypes.c_uint64]),

@@ -266,6 +266,92 @@ def w8a8_gemm_dynamic(a: torch.Tensor, w_nk: torch.Tensor, w_scale: torch.Tensor
     return out
 
 
+# ---------------------------------------------------------------------------
+# FP8 (e4m3) W8A8
+# ---------------------------------------------------------------------------
+_FP8_MODES = {"per_token": L.CB_FP8_PER_TOKEN, "per_tensor": L.CB_FP8_PER_TENSOR_DYNAMIC, "static": L.CB_FP8_STATIC}
+
+
+def quant_act_fp8(a: torch.Tensor, mode: str = "per_token", scale: torch.Tensor | None = None,
+                  q: torch.Tensor | None = None):
+    """e4m3 quantization of ``a`` ([M, K] or [B, M, K], f16/bf16).
+
+    mode "per_token": one dynamic scale per row (fp32, B*M); "per_tensor": one
+    dynamic scale per batch entry (B); "static": ``scale`` (B elements) given.
+    Returns ``(q float8_e4m3fn like a, scale)``.
+    """
+    _require_cuda(a, scale, q)
+    a3 = _as3d(a)
+    B, M, K = a3.shape
+    if a3.stride(2) != 1:
+        raise ValueError("activations must be contiguous along K")
+    code_mode = _FP8_MODES.get(mode)
+    if code_mode is None:
+        raise ValueError(f"mode must be one of {sorted(_FP8_MODES)}")
+    if mode == "static":
+        if scale is None or scale.numel() < B or scale.dtype != torch.float32 or not scale.is_contiguous():
+            raise ValueError("static mode needs a contiguous fp32 scale with one value per batch entry")
+    elif scale is None:
+        scale = torch.empty(B * M if mode == "per_token" else B, dtype=torch.float32, device=a.device)
+    if q is None:
+        q = torch.empty(a.shape, dtype=torch.float8_e4m3fn, device=a.device)
+    q3 = _as3d(q)
+    if q3.shape != a3.shape or q.element_size() != 1 or q3.stride(2) != 1:
+        raise ValueError("q must be a 1-byte tensor shaped like a, contiguous along K")
+    code = L.load().cb_quant_act_fp8(a3.data_ptr(), dtype_code(a.dtype), B, M, K, a3.stride(0), a3.stride(1),
+                                     q3.data_ptr(), q3.stride(0), q3.stride(1), scale.data_ptr(),
+                                     M if mode == "per_token" else 1, code_mode, _stream(a.device))
+    L.check("cb_quant_act_fp8", code)
+    return q, scale
+
+
+def fp8_gemm(aq: torch.Tensor, w_nk: torch.Tensor, a_scale: torch.Tensor, w_scale: torch.Tensor,
+             out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
+             bias: torch.Tensor | None = None) -> torch.Tensor:
+    """``out = ((aq @ w_nk^T) * a_scale) * w_scale (+ bias)`` on e4m3 operands, fp32 accumulation.
+
+    aq: e4m3 [M, K] / [B, M, K]; w_nk: e4m3 [N, K] / [B, N, K] (K contiguous).
+    a_scale: B*M values (per token) or B (per tensor); w_scale: B*N (per channel)
+    or B (per tensor); bias: optional [N] added in fp32 before the rounding.
+    """
+    _require_cuda(aq, w_nk, a_scale, w_scale, out, bias)
+    a3, w3 = _as3d(aq), _as3d(w_nk)
+    B, M, K = a3.shape
+    Bw, N, Kw = w3.shape
+    if aq.element_size() != 1 or w_nk.element_size() != 1:
+        raise ValueError("fp8_gemm expects 1-byte e4m3 operands")
+    if Kw != K or Bw != B:
+        raise ValueError(f"shape mismatch: aq {tuple(a3.shape)} vs w {tuple(w3.shape)}")
+    if a3.stride(2) != 1 or w3.stride(2) != 1:
+        raise ValueError("operands must be contiguous along K (weights K-major [N, K])")
+    for t, nm in ((a_scale, "a_scale"), (w_scale, "w_scale")):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError(f"{nm} must be contiguous fp32")
+    if a_scale.numel() not in (B, B * M):
+        raise ValueError("a_scale must have B*M (per token) or B (per tensor) elements")
+    if w_scale.numel() not in (B, B * N):
+        raise ValueError("w_scale must have B*N (per channel) or B (per tensor) elements")
+    a_pt = a_scale.numel() == B and B * M != B
+    w_pt = w_scale.numel() == B and B * N != B
+    if bias is not None and (bias.numel() != N or not bias.is_contiguous()):
+        raise ValueError("bias must be a contiguous [N] tensor")
+    if out is None:
+        out = torch.empty((B, M, N) if aq.dim() == 3 else (M, N), dtype=out_dtype, device=aq.device)
+    o3 = _as3d(out)
+    if o3.shape != (B, M, N) or o3.stride(2) != 1:
+        raise ValueError("out must be [B, M, N] contiguous along N")
+    nbytes = workspace_bytes(L.CB_OP_W8A8, B, M, N, K)
+    ws = POOL.get(nbytes, aq.device)
+    st = _strides(a3.stride(0), a3.stride(1), w3.stride(0), w3.stride(1), o3.stride(0), o3.stride(1),
+                  1 if a_pt else M, 1 if w_pt else N)
+    code = L.load().cb_fp8_gemm(a3.data_ptr(), a_scale.data_ptr(), int(a_pt), w3.data_ptr(), w_scale.data_ptr(),
+                                int(w_pt), _ptr(bias), dtype_code(bias.dtype) if bias is not None else 0,
+                                o3.data_ptr(), dtype_code(out.dtype), B, M, N, K, st, ws.data_ptr(), ws.numel(),
+                                _stream(aq.device))
+    L.check("cb_fp8_gemm", code)
+    return out
+
+
 def repack_w8_kmajor(w_kn: torch.Tensor) -> torch.Tensor:
     """int8 [B, K, N] / [K, N] (N contiguous) -> contiguous [B, N, K] / [N, K]."""
     _require_cuda(w_kn)

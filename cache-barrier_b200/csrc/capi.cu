@@ -390,6 +390,57 @@ int cb_w8a8_gemm_dynamic(const void* a, int a_dtype, int8_t* q_buf, float* s_buf
   return launch_w8a8(L, s);
 }
 
+int cb_quant_act_fp8(const void* a, int a_dtype, int64_t batch, int64_t M, int64_t K, int64_t a_stride_b,
+                     int64_t a_stride_m, uint8_t* q, int64_t q_stride_b, int64_t q_stride_m, float* scale,
+                     int64_t scale_stride_b, int mode, cb_stream_t stream) {
+  if (batch < 0 || M < 0 || K < 0) return CB_ERR_INVALID_ARG;
+  if (batch * M * K == 0) return CB_OK;
+  if (!a || !q || !scale) return CB_ERR_INVALID_ARG;
+  if (a_dtype != CB_DTYPE_F16 && a_dtype != CB_DTYPE_BF16) return CB_ERR_DTYPE;
+  if (K > 0x7fffffffLL || M > 0x7fffffffLL || batch > 0xffffLL) return CB_ERR_TOO_LARGE;
+  return launch_act_quant_fp8(a, a_dtype, batch, M, K, a_stride_b, a_stride_m, q, q_stride_b, q_stride_m, scale,
+                              scale_stride_b, mode, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int cb_fp8_gemm(const uint8_t* aq, const float* a_scale, int a_scale_per_tensor, const uint8_t* w,
+                const float* w_scale, int w_scale_per_tensor, const void* bias, int bias_dtype, void* out,
+                int out_dtype, int64_t batch, int64_t M, int64_t N, int64_t K, const int64_t* strides,
+                void* workspace, size_t workspace_bytes, cb_stream_t stream) {
+  int v = validate_w8a8(reinterpret_cast<const int8_t*>(aq), reinterpret_cast<const int8_t*>(w), out, out_dtype,
+                        batch, M, N, K, strides);
+  if (v != CB_OK || batch * M * N == 0) return v;
+  if (!a_scale || !w_scale) return CB_ERR_INVALID_ARG;
+  if (bias && !valid_out_dtype(bias_dtype)) return CB_ERR_DTYPE;
+  W8A8Launch L = {};
+  L.aq = reinterpret_cast<const int8_t*>(aq);
+  L.a_scale = a_scale;
+  L.w = reinterpret_cast<const int8_t*>(w);
+  L.w_scale = w_scale;
+  L.out = out;
+  L.out_dtype = out_dtype;
+  L.batch = batch;
+  L.M = M;
+  L.N = N;
+  L.K = K;
+  L.aq_sb = strides[0];
+  L.aq_sm = strides[1];
+  L.w_sb = strides[2];
+  L.w_sn = strides[3];
+  L.out_sb = strides[4];
+  L.out_sm = strides[5];
+  L.as_sb = strides[6];
+  L.ws_sb = strides[7];
+  L.fp8 = 1;
+  L.scale_per_tensor_a = a_scale_per_tensor ? 1 : 0;
+  L.scale_per_tensor_w = w_scale_per_tensor ? 1 : 0;
+  L.bias = bias;
+  L.bias_dtype = bias_dtype;
+  L.bias_sb = 0;
+  L.workspace = workspace;
+  L.workspace_bytes = workspace_bytes;
+  return launch_w8a8(L, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int cb_w4a16_gemm(const void* a, int a_dtype, const uint8_t* w_native, const void* scales, int scale_dtype,
                   int64_t group_size, void* out, int out_dtype, int64_t batch, int64_t M, int64_t N, int64_t K,
                   const int64_t* strides, void* workspace, size_t workspace_bytes, cb_stream_t stream) {

@@ -93,6 +93,12 @@ int validate_w8a8(const int8_t* aq, const int8_t* w, void* out, int out_dtype, i
 // ---- launchers (validated arguments) ----
 int launch_act_quant(const void* a, int a_dtype, int64_t batch, int64_t M, int64_t K, int64_t a_sb, int64_t a_sm,
                      int8_t* q, int64_t q_sb, int64_t q_sm, float* scale, int64_t s_sb, cudaStream_t stream);
+// e4m3 quantization of activations: mode CB_FP8_PER_TOKEN (scale per row),
+// CB_FP8_PER_TENSOR_DYNAMIC (one scale per batch entry, from its amax) or
+// CB_FP8_STATIC (scale[b * s_sb] given).
+int launch_act_quant_fp8(const void* a, int a_dtype, int64_t batch, int64_t M, int64_t K, int64_t a_sb, int64_t a_sm,
+                         uint8_t* q, int64_t q_sb, int64_t q_sm, float* scale, int64_t s_sb, int mode,
+                         cudaStream_t stream);
 
 struct W8A8Launch {
   const int8_t* aq;
@@ -106,6 +112,9 @@ struct W8A8Launch {
   int64_t aq_sb, aq_sm, w_sb, w_sn, out_sb, out_sm, as_sb, ws_sb;
   int raw_f32;            // 1: out = (float)acc, no scales (W4A4 path)
   int unsigned_operands;  // 1: both operands are uint8 (W4A4 reference-wrap mode)
+  int fp8;                // 1: both operands are e4m3 fp8 (fp32 accumulators; acc_out unused)
+  int scale_per_tensor_a; // 1: a_scale holds one value per batch entry (else one per token)
+  int scale_per_tensor_w; // 1: w_scale holds one value per batch entry (else one per output channel)
   const void* bias;       // optional [batch, N] bias (f16/bf16/f32) added in fp32 before rounding
   int bias_dtype;
   int64_t bias_sb;

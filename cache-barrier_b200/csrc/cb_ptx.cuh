@@ -204,6 +204,10 @@ __host__ __device__ constexpr uint32_t idesc_i8_s32(int M, int N) {
 __host__ __device__ constexpr uint32_t idesc_u8_s32(int M, int N) {
   return (2u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
+// kind::f8f6f4 with both operands e4m3 (format 0), f32 accumulate.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
 // ab_fmt: 0 = f16, 1 = bf16.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, int ab_fmt) {
   return (1u << 4) | (static_cast<uint32_t>(ab_fmt) << 7) | (static_cast<uint32_t>(ab_fmt) << 10) |
@@ -219,6 +223,18 @@ __device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 8-bit floating-point operands (kind::f8f6f4; formats in the instruction
+// descriptor), both from shared memory, K = 32 per instruction.
+__device__ __forceinline__ void mma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

@@ -30,6 +30,8 @@
 #include "cb_internal.h"
 #include "cb_ptx.cuh"
 
+#include <type_traits>
+
 namespace cb {
 namespace {
 
@@ -40,15 +42,43 @@ constexpr int kWaiterWarp = 6;
 constexpr int kHandoffBar = 2;  // named barrier: MMA warp + stage waiter (barrier 1 is the epilogue's)
 constexpr uint32_t kWTileBytes = kBlockN * kBlockK;
 
+// Operand kinds: signed int8 (W8A8), unsigned 8-bit (the W4A4 reference-wrap
+// mode), both with int32 accumulators; e4m3 fp8 with fp32 accumulators. All are
+// 8-bit operands, so the tiles, ring and MMA K (32) are the same.
+constexpr int kKindS8 = 0, kKindU8 = 1, kKindE4M3 = 2;
+template <int KIND>
+struct AccOf {
+  using T = int32_t;
+};
+template <>
+struct AccOf<kKindE4M3> {
+  using T = float;
+};
+__device__ __forceinline__ float acc_f(int32_t v) { return __int2float_rn(v); }
+__device__ __forceinline__ float acc_f(float v) { return v; }
+template <typename Acc>
+__device__ __forceinline__ Acc acc_from_bits(uint32_t b);
+template <>
+__device__ __forceinline__ int32_t acc_from_bits<int32_t>(uint32_t b) {
+  return static_cast<int32_t>(b);
+}
+template <>
+__device__ __forceinline__ float acc_from_bits<float>(uint32_t b) {
+  return __uint_as_float(b);
+}
+// Keeps a value live at this point (the compiler may not sink its load past it).
+__device__ __forceinline__ void keep(int32_t v) { asm volatile("" ::"r"(v)); }
+__device__ __forceinline__ void keep(float v) { asm volatile("" ::"f"(v)); }
+
 struct Params {
   int M, N, K, H;
   int n_tiles, m_tiles, kb_per_tile;
   int stages;
   StreamK sk;
   const float* a_scale;
-  long long as_sb;
+  long long as_sb, as_sm;  // a_scale[h * as_sb + m * as_sm] (as_sm = 0: one scale per batch entry)
   const float* w_scale;
-  long long ws_sb;
+  long long ws_sb, ws_sn;  // w_scale[h * ws_sb + n * ws_sn]
   void* out;
   int out_dtype;
   long long out_sb, out_sm;
@@ -59,7 +89,7 @@ struct Params {
   long long bias_sb;
   unsigned long long dbg_wait_ns;  // test hook: nonzero = wait this long on a flag nothing sets
   int vec_out;  // 16-bit output, N % 8 == 0, 16-byte aligned rows, no acc_out: vector stores
-  int32_t* partials;  // [grid][2][TN][128]
+  void* partials;  // [grid][2][TN][128] accumulators (int32 or fp32)
   int* counters;      // [grid]
   int* status;
 };
@@ -71,35 +101,38 @@ __device__ __forceinline__ void decode_tile(const Params& p, long long tile, int
   h = static_cast<int>(r / p.n_tiles);
 }
 
-template <int TN>
-__device__ __forceinline__ void emit_row(const Params& p, int h, int n, int m0, int t0, const int32_t (&v)[16]) {
+template <int TN, typename Acc>
+__device__ __forceinline__ void emit_row(const Params& p, int h, int n, int m0, int t0, const Acc (&v)[16]) {
   if (n >= p.N) return;
   // All scale loads are issued before any store: a load placed after a store
   // that may alias it would otherwise wait for the previous iteration.
-  const float ws = p.raw_f32 ? 1.0f : __ldg(p.w_scale + h * p.ws_sb + n);
+  const float ws = p.raw_f32 ? 1.0f : __ldg(p.w_scale + h * p.ws_sb + n * p.ws_sn);
   const float bv = p.bias ? load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n) : 0.0f;
   float as[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int m = m0 + t0 + j;
-    as[j] = (!p.raw_f32 && m < p.M) ? __ldg(p.a_scale + h * p.as_sb + m) : 1.0f;
+    as[j] = (!p.raw_f32 && m < p.M) ? __ldg(p.a_scale + h * p.as_sb + m * p.as_sm) : 1.0f;
   }
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int m = m0 + t0 + j;
     if (m < p.M) {
       const long long idx = h * p.out_sb + static_cast<long long>(m) * p.out_sm + n;
-      float f = __int2float_rn(v[j]);
+      float f = acc_f(v[j]);
       if (!p.raw_f32) f = __fmul_rn(__fmul_rn(f, as[j]), ws);
       if (p.bias) f = __fadd_rn(f, bv);
       store_elem(p.out, p.out_dtype, idx, f);
-      if (p.acc_out) p.acc_out[idx] = v[j];
+      if constexpr (std::is_same<Acc, int32_t>::value) {
+        if (p.acc_out) p.acc_out[idx] = v[j];
+      }
     }
   }
 }
 
 // emit_row with the scales (and bias) already in registers (loaded when the segment began).
-__device__ __forceinline__ void emit_row_pre(const Params& p, int h, int n, int m0, int t0, const int32_t (&v)[16],
+template <typename Acc>
+__device__ __forceinline__ void emit_row_pre(const Params& p, int h, int n, int m0, int t0, const Acc (&v)[16],
                                              float ws, float bv, const float (&as)[16]) {
   if (n >= p.N) return;
 #pragma unroll
@@ -107,11 +140,13 @@ __device__ __forceinline__ void emit_row_pre(const Params& p, int h, int n, int 
     const int m = m0 + t0 + j;
     if (m < p.M) {
       const long long idx = h * p.out_sb + static_cast<long long>(m) * p.out_sm + n;
-      float f = __int2float_rn(v[j]);
+      float f = acc_f(v[j]);
       if (!p.raw_f32) f = __fmul_rn(__fmul_rn(f, as[j]), ws);
       if (p.bias) f = __fadd_rn(f, bv);
       store_elem(p.out, p.out_dtype, idx, f);
-      if (p.acc_out) p.acc_out[idx] = v[j];
+      if constexpr (std::is_same<Acc, int32_t>::value) {
+        if (p.acc_out) p.acc_out[idx] = v[j];
+      }
     }
   }
 }
@@ -122,14 +157,14 @@ __device__ __forceinline__ void emit_row_pre(const Params& p, int h, int n, int 
 // column-per-thread form. Those stores set the kernel's tail: the collector's
 // sum-and-store after its last MMA took ~1 / 1.8 / 3.3 us at T = 1 / 16 / 32.
 // Same arithmetic and rounding as emit_row_pre.
-template <int OUT_BF16>
+template <int OUT_BF16, typename Acc>
 __device__ __forceinline__ void emit_chunk_vec(const Params& p, int h, int n_warp0, int lane, int m0, int t0,
-                                               const int32_t (&v)[16], float ws, float bv, const float (&as)[16],
+                                               const Acc (&v)[16], float ws, float bv, const float (&as)[16],
                                                uint16_t* stg) {
   const bool has_bias = p.bias != nullptr;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    float f = __fmul_rn(__fmul_rn(__int2float_rn(v[j]), as[j]), ws);
+    float f = __fmul_rn(__fmul_rn(acc_f(v[j]), as[j]), ws);
     if (has_bias) f = __fadd_rn(f, bv);
     stg[j * 32 + lane] =
         OUT_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(f)) : __half_as_ushort(__float2half_rn(f));
@@ -152,41 +187,41 @@ __device__ __forceinline__ void emit_chunk_vec(const Params& p, int h, int n_war
 // Warp-collective store of one 16-token chunk for the paths without preloaded
 // scales (token tiles above 32): loads the scales as emit_row does, then takes
 // the vector path for 16-bit outputs.
-template <int TN>
+template <int TN, typename Acc>
 __device__ __forceinline__ void emit_row_any(const Params& p, int h, int n, int lane, int m0, int t0,
-                                             const int32_t (&v)[16], uint16_t* stg) {
+                                             const Acc (&v)[16], uint16_t* stg) {
   if (!p.vec_out) {
-    emit_row<TN>(p, h, n, m0, t0, v);
+    emit_row<TN, Acc>(p, h, n, m0, t0, v);
     return;
   }
-  const float ws = n < p.N ? __ldg(p.w_scale + h * p.ws_sb + n) : 1.0f;
+  const float ws = n < p.N ? __ldg(p.w_scale + h * p.ws_sb + n * p.ws_sn) : 1.0f;
   const float bv = (p.bias && n < p.N) ? load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n) : 0.0f;
   float as[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int m = m0 + t0 + j;
-    as[j] = m < p.M ? __ldg(p.a_scale + h * p.as_sb + m) : 1.0f;
+    as[j] = m < p.M ? __ldg(p.a_scale + h * p.as_sb + m * p.as_sm) : 1.0f;
   }
   if (p.out_dtype == CB_DTYPE_BF16)
-    emit_chunk_vec<1>(p, h, n - lane, lane, m0, t0, v, ws, bv, as, stg);
+    emit_chunk_vec<1, Acc>(p, h, n - lane, lane, m0, t0, v, ws, bv, as, stg);
   else
-    emit_chunk_vec<0>(p, h, n - lane, lane, m0, t0, v, ws, bv, as, stg);
+    emit_chunk_vec<0, Acc>(p, h, n - lane, lane, m0, t0, v, ws, bv, as, stg);
 }
 
 // Adds the published parts of contributors [c_lo, c_hi] (each its first
 // segment, slot kind 0) for chunk c of this thread's row; loads of four
 // contributors are in flight together.
-template <int TN>
-__device__ __forceinline__ void sum_published(const Params& p, int c_lo, int c_hi, int c, int row,
-                                              int32_t (&v)[16]) {
+template <int TN, typename Acc>
+__device__ __forceinline__ void sum_published(const Params& p, int c_lo, int c_hi, int c, int row, Acc (&v)[16]) {
   for (int cc = c_lo; cc <= c_hi; cc += 4) {
-    int32_t part[4][16];
+    Acc part[4][16];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int c2 = cc + u;
-      const int32_t* src = p.partials + static_cast<long long>(c2 * 2) * TN * kBlockN + (c * 16) * kBlockN + row;
+      const Acc* src =
+          static_cast<const Acc*>(p.partials) + static_cast<long long>(c2 * 2) * TN * kBlockN + (c * 16) * kBlockN + row;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) part[u][j] = c2 <= c_hi ? __ldcg(src + j * kBlockN) : 0;
+      for (int j = 0; j < 16; ++j) part[u][j] = c2 <= c_hi ? __ldcg(src + j * kBlockN) : Acc(0);
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u)
@@ -195,10 +230,11 @@ __device__ __forceinline__ void sum_published(const Params& p, int c_lo, int c_h
   }
 }
 
-template <int TN, bool kUnsigned>
+template <int TN, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                      const Params p) {
+  using Acc = typename AccOf<KIND>::T;
   constexpr uint32_t kATileBytes = TN * kBlockK;
   constexpr uint32_t kStageBytes = kWTileBytes + kATileBytes;
   constexpr uint32_t kTmemCols = TN < 32 ? 32 : TN;
@@ -313,7 +349,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // hands each k-block over through a named barrier (no shared memory); the
     // barrier's OR also carries a failed wait of either side, so both warps
     // leave their loops at the same k-block.
-    const uint32_t idesc = kUnsigned ? idesc_u8_s32(kBlockN, TN) : idesc_i8_s32(kBlockN, TN);
+    const uint32_t idesc = KIND == kKindU8     ? idesc_u8_s32(kBlockN, TN)
+                           : KIND == kKindE4M3 ? idesc_e4m3_f32(kBlockN, TN)
+                                               : idesc_i8_s32(kBlockN, TN);
     int stage = 0;
     uint32_t acc_phase = 0;
     int consumed = 0;
@@ -341,8 +379,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t aa = smem_u32(smem_a + stage * kATileBytes);
 #pragma unroll
           for (int kk = 0; kk < kBlockK / 32; ++kk) {
-            mma_i8_ss(tmem_d, smem_desc_sw128(wa + kk * 32), smem_desc_sw128(aa + kk * 32), idesc,
-                      (first && kk == 0) ? 0u : 1u);
+            if constexpr (KIND == kKindE4M3)
+              mma_f8_ss(tmem_d, smem_desc_sw128(wa + kk * 32), smem_desc_sw128(aa + kk * 32), idesc,
+                        (first && kk == 0) ? 0u : 1u);
+            else
+              mma_i8_ss(tmem_d, smem_desc_sw128(wa + kk * 32), smem_desc_sw128(aa + kk * 32), idesc,
+                        (first && kk == 0) ? 0u : 1u);
           }
           mma_commit(&empty_bar[stage]);
         }
@@ -432,8 +474,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool stores = whole || collect;
 #pragma unroll
         for (int j = 0; j < TN; ++j)
-          as_pre[j] = (stores && !p.raw_f32 && m0 + j < p.M) ? __ldg(p.a_scale + h * p.as_sb + m0 + j) : 1.0f;
-        if (stores && !p.raw_f32 && n < p.N) ws_pre = __ldg(p.w_scale + h * p.ws_sb + n);
+          as_pre[j] = (stores && !p.raw_f32 && m0 + j < p.M) ? __ldg(p.a_scale + h * p.as_sb + (m0 + j) * p.as_sm) : 1.0f;
+        if (stores && !p.raw_f32 && n < p.N) ws_pre = __ldg(p.w_scale + h * p.ws_sb + n * p.ws_sn);
         if (stores && p.bias && n < p.N) bias_pre = load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n);
         // Consume the values here, so the compiler cannot sink the loads to
         // their use after the last MMA.
@@ -442,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("" ::"f"(ws_pre));
         asm volatile("" ::"f"(bias_pre));
       }
-      int32_t other[kPrefetch ? TN : 1];
+      Acc other[kPrefetch ? TN : 1];
       bool others_ready = true;
       if (collect) {
         // The other contributors handled this tile at the start of their ranges;
@@ -453,14 +495,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         others_ready = sh_is_last != 0;
         if constexpr (kPrefetch) {
 #pragma unroll
-          for (int j = 0; j < TN; ++j) other[j] = 0;
+          for (int j = 0; j < TN; ++j) other[j] = Acc(0);
           if (others_ready) {
 #pragma unroll
             for (int c = 0; c < TN / 16; ++c) {
-              int32_t v[16];
+              Acc v[16];
 #pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] = 0;
-              sum_published<TN>(p, c_first + 1, c_last, c, row, v);
+              for (int j = 0; j < 16; ++j) v[j] = Acc(0);
+              sum_published<TN, Acc>(p, c_first + 1, c_last, c, row, v);
 #pragma unroll
               for (int j = 0; j < 16; ++j) other[c * 16 + j] = v[j];
             }
@@ -468,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Complete the partial sums now, while this CTA's last MMAs run; the
           // compiler would otherwise sink the loads to their use after the wait.
 #pragma unroll
-          for (int j = 0; j < TN; ++j) asm volatile("" ::"r"(other[j]));
+          for (int j = 0; j < TN; ++j) keep(other[j]);
         }
       }
       const bool got = mbar_wait(&tfull_bar, acc_phase, abort_ptr, p.status);
@@ -485,21 +527,21 @@ __global__ void __launch_bounds__(kThreads, 1)
               __syncwarp();
               tmem_ld16(lane_addr + c * 16, r);
               tmem_ld_wait();
-              int32_t v[16];
+              Acc v[16];
               float as16[16];
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
-                v[j] = static_cast<int32_t>(r[j]);
+                v[j] = acc_from_bits<Acc>(r[j]);
                 as16[j] = as_pre[c * 16 + j];
               }
               if (p.vec_out) {
                 uint16_t* stg = epi_stage + (warp - 2) * 512;
                 if (p.out_dtype == CB_DTYPE_BF16)
-                  emit_chunk_vec<1>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
+                  emit_chunk_vec<1, Acc>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
                 else
-                  emit_chunk_vec<0>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
+                  emit_chunk_vec<0, Acc>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
               } else {
-                emit_row_pre(p, h, n, m0, c * 16, v, ws_pre, bias_pre, as16);
+                emit_row_pre<Acc>(p, h, n, m0, c * 16, v, ws_pre, bias_pre, as16);
               }
             }
           } else {
@@ -509,10 +551,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               __syncwarp();
               tmem_ld16(lane_addr + c * 16, r);
               tmem_ld_wait();
-              int32_t v[16];
+              Acc v[16];
 #pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] = static_cast<int32_t>(r[j]);
-              emit_row_any<TN>(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - 2) * 512);
+              for (int j = 0; j < 16; ++j) v[j] = acc_from_bits<Acc>(r[j]);
+              emit_row_any<TN, Acc>(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - 2) * 512);
             }
           }
         }
@@ -523,7 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Partial tile, not its first contributor: publish this CTA's part
         // (this is the CTA's first segment, long before the collector needs it).
         const int slot = blockIdx.x * 2 + (first_seg ? 0 : 1);
-        int32_t* dst = p.partials + static_cast<long long>(slot) * TN * kBlockN;
+        uint32_t* dst = static_cast<uint32_t*>(p.partials) + static_cast<long long>(slot) * TN * kBlockN;
         if (live) {
 #pragma unroll 1
           for (int c = 0; c < TN / 16; ++c) {
@@ -532,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld16(lane_addr + c * 16, r);
             tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) dst[(c * 16 + j) * kBlockN + row] = static_cast<int32_t>(r[j]);
+            for (int j = 0; j < 16; ++j) dst[(c * 16 + j) * kBlockN + row] = r[j];  // raw accumulator bits
           }
         }
         tc_fence_before();
@@ -552,21 +594,21 @@ __global__ void __launch_bounds__(kThreads, 1)
               __syncwarp();
               tmem_ld16(lane_addr + c * 16, r);
               tmem_ld_wait();
-              int32_t v[16];
+              Acc v[16];
               float as16[16];
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
-                v[j] = static_cast<int32_t>(r[j]) + other[c * 16 + j];
+                v[j] = acc_from_bits<Acc>(r[j]) + other[c * 16 + j];
                 as16[j] = as_pre[c * 16 + j];
               }
               if (p.vec_out) {
                 uint16_t* stg = epi_stage + (warp - 2) * 512;
                 if (p.out_dtype == CB_DTYPE_BF16)
-                  emit_chunk_vec<1>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
+                  emit_chunk_vec<1, Acc>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
                 else
-                  emit_chunk_vec<0>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
+                  emit_chunk_vec<0, Acc>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
               } else {
-                emit_row_pre(p, h, n, m0, c * 16, v, ws_pre, bias_pre, as16);
+                emit_row_pre<Acc>(p, h, n, m0, c * 16, v, ws_pre, bias_pre, as16);
               }
             }
           } else {
@@ -576,11 +618,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               __syncwarp();
               tmem_ld16(lane_addr + c * 16, r);
               tmem_ld_wait();
-              int32_t v[16];
+              Acc v[16];
 #pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] = static_cast<int32_t>(r[j]);
-              sum_published<TN>(p, c_first + 1, c_last, c, row, v);
-              emit_row_any<TN>(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - 2) * 512);
+              for (int j = 0; j < 16; ++j) v[j] = acc_from_bits<Acc>(r[j]);
+              sum_published<TN, Acc>(p, c_first + 1, c_last, c, row, v);
+              emit_row_any<TN, Acc>(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - 2) * 512);
             }
           }
           if (threadIdx.x == 64) p.counters[c_first] = 0;  // next launch starts from zero
@@ -608,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int TN, bool kUnsigned>
+template <int TN, int KIND>
 int launch_tn(const W8A8Launch& L, cudaStream_t stream, int grid, int stages, const Params& prm) {
   CUtensorMap tw, ta;
   int st = encode_tmap_3d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.w, static_cast<uint64_t>(L.K),
@@ -625,7 +667,7 @@ int launch_tn(const W8A8Launch& L, cudaStream_t stream, int grid, int stages, co
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_dev != dev || configured_smem < smem) {
-    cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_kernel<TN, kUnsigned>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_kernel<TN, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return CB_ERR_CUDA;
     configured_dev = dev;
@@ -641,22 +683,22 @@ int launch_tn(const W8A8Launch& L, cudaStream_t stream, int grid, int stages, co
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, w8a8_gemm_kernel<TN, kUnsigned>, tw, ta, prm));
+  return cuda_status(cudaLaunchKernelEx(&cfg, w8a8_gemm_kernel<TN, KIND>, tw, ta, prm));
 }
 
-template <bool kUnsigned>
+template <int KIND>
 int dispatch_tn(const W8A8Launch& L, cudaStream_t stream, int TN, int grid, int stages, const Params& p) {
   switch (TN) {
     case 16:
-      return launch_tn<16, kUnsigned>(L, stream, grid, stages, p);
+      return launch_tn<16, KIND>(L, stream, grid, stages, p);
     case 32:
-      return launch_tn<32, kUnsigned>(L, stream, grid, stages, p);
+      return launch_tn<32, KIND>(L, stream, grid, stages, p);
     case 64:
-      return launch_tn<64, kUnsigned>(L, stream, grid, stages, p);
+      return launch_tn<64, KIND>(L, stream, grid, stages, p);
     case 128:
-      return launch_tn<128, kUnsigned>(L, stream, grid, stages, p);
+      return launch_tn<128, KIND>(L, stream, grid, stages, p);
     default:
-      return launch_tn<256, kUnsigned>(L, stream, grid, stages, p);
+      return launch_tn<256, KIND>(L, stream, grid, stages, p);
   }
 }
 
@@ -701,8 +743,10 @@ int launch_w8a8(const W8A8Launch& L, cudaStream_t stream) {
   p.sk.kb_per_tile = p.kb_per_tile;
   p.a_scale = L.a_scale;
   p.as_sb = L.as_sb;
+  p.as_sm = L.scale_per_tensor_a ? 0 : 1;
   p.w_scale = L.w_scale;
   p.ws_sb = L.ws_sb;
+  p.ws_sn = L.scale_per_tensor_w ? 0 : 1;
   p.out = L.out;
   p.out_dtype = L.out_dtype;
   p.out_sb = L.out_sb;
@@ -719,11 +763,12 @@ int launch_w8a8(const W8A8Launch& L, cudaStream_t stream) {
                   ? 1
                   : 0;
   Workspace ws = carve_workspace(L.workspace, grid);
-  p.partials = static_cast<int32_t*>(ws.partials);
+  p.partials = ws.partials;
   p.counters = ws.counters;
   p.status = ws.status;
-  if (L.unsigned_operands) return dispatch_tn<true>(L, stream, TN, grid, stages, p);
-  return dispatch_tn<false>(L, stream, TN, grid, stages, p);
+  if (L.fp8) return dispatch_tn<kKindE4M3>(L, stream, TN, grid, stages, p);
+  if (L.unsigned_operands) return dispatch_tn<kKindU8>(L, stream, TN, grid, stages, p);
+  return dispatch_tn<kKindS8>(L, stream, TN, grid, stages, p);
 }
 
 }  // namespace cb

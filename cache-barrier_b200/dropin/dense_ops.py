@@ -24,6 +24,10 @@ call shapes for the int8 W8A8 and int4 W4A16 paths:
   apply_w4a16_linear(x, w_native, scales, N, K, bias=None)
       x [M, K] @ dequant(w)^T -> [M, N] in x's dtype; takes the place of
       apply_fp8_marlin_linear(x, qw, s, workspace, N, K, None).
+  scaled_fp8_quant(x, scale=None, use_per_token_if_dynamic=False) -> (q e4m3 [M, K], scale)
+      e4m3 activations (per-tensor dynamic, per-token dynamic or static), and
+      cutlass_scaled_mm on e4m3 a / b: the fp8 W8A8 path the reference's dense
+      harnesses time (profiling/dense_qwen/bench_l2_boundary.py:54-57, 66-68).
   scaled_fp4_quant(x, global_scale) -> (q uint8 [M, K/2], scales e4m3 [pad(M,128), pad(K/16,4)])
   cutlass_scaled_fp4_mm(a, b, block_scale_a, block_scale_b, alpha, out_dtype)
       NVFP4 in vLLM's call shapes and tensor formats (the reference's native-FP4
@@ -59,8 +63,10 @@ def cutlass_scaled_mm(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor, s
                       out_dtype: torch.dtype, bias: torch.Tensor | None = None) -> torch.Tensor:
     if a.dim() != 2 or b.dim() != 2:
         raise ValueError("cutlass_scaled_mm expects 2-D a [M, K] and b [K, N]")
+    if a.dtype == torch.float8_e4m3fn and b.dtype == torch.float8_e4m3fn:
+        return _scaled_mm_fp8(a, b, scale_a, scale_b, out_dtype, bias)
     if a.dtype != torch.int8 or b.dtype != torch.int8:
-        raise ValueError("this drop-in implements the int8 path (a and b int8)")
+        raise ValueError("this drop-in implements the int8 and e4m3 paths (a and b both int8 or both e4m3)")
     M, K = a.shape
     Kb, N = b.shape
     if Kb != K:
@@ -73,6 +79,42 @@ def cutlass_scaled_mm(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor, s
     # vLLM adds the bias in its fp32 epilogue, before the one rounding to out_dtype; so does the kernel
     return ops.w8a8_gemm(a, w_nk, _per_row(scale_a, M, "scale_a"), _per_row(scale_b, N, "scale_b"),
                          out_dtype=out_dtype, bias=None if bias is None else bias.reshape(N).contiguous())
+
+
+def _scaled_mm_fp8(a, b, scale_a, scale_b, out_dtype, bias):
+    M, K = a.shape
+    Kb, N = b.shape
+    if Kb != K:
+        raise ValueError(f"shape mismatch: a {tuple(a.shape)} b {tuple(b.shape)}")
+    if out_dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("out_dtype must be bfloat16 or float16")
+    if b.stride(0) != 1:
+        raise ValueError("b must be the column-major [K, N] view of a K-major [N, K] e4m3 weight (as vLLM takes it)")
+    sa, sb = scale_a.reshape(-1).float().contiguous(), scale_b.reshape(-1).float().contiguous()
+    if sa.numel() not in (1, M) or sb.numel() not in (1, N):
+        raise ValueError("scale_a must be per-tensor or per-token, scale_b per-tensor or per-channel")
+    if bias is not None and (bias.numel() != N or bias.dtype not in (torch.bfloat16, torch.float16, torch.float32)):
+        raise ValueError(f"bias must have N={N} elements of a floating dtype")
+    return ops.fp8_gemm(a, b.t(), sa, sb, out_dtype=out_dtype,
+                        bias=None if bias is None else bias.reshape(N).contiguous())
+
+
+def scaled_fp8_quant(x: torch.Tensor, scale: torch.Tensor | None = None, num_token_padding=None, scale_ub=None,
+                     use_per_token_if_dynamic: bool = False, output=None):
+    """vLLM's scaled_fp8_quant: e4m3 values and the fp32 scale ([1] per tensor, [M, 1] per token).
+    Dynamic scale = max(amax / 448, 1 / (448 * 512)); q = e4m3(clamp(x / scale, +-448))."""
+    if num_token_padding is not None or scale_ub is not None:
+        raise NotImplementedError("token padding and scale upper bounds are not provided")
+    if x.dim() != 2:
+        raise ValueError("x must be [M, K]")
+    if scale is not None:
+        q, s = ops.quant_act_fp8(x, "static", scale=scale.reshape(1).float().contiguous(), q=output)
+        return q, s.view(1)
+    if use_per_token_if_dynamic:
+        q, s = ops.quant_act_fp8(x, "per_token", q=output)
+        return q, s.view(-1, 1)
+    q, s = ops.quant_act_fp8(x, "per_tensor", q=output)
+    return q, s.view(1)
 
 
 def scaled_int8_quant(x: torch.Tensor, scale: torch.Tensor | None = None, azp=None, symmetric: bool = True):

@@ -189,6 +189,38 @@ CB_API int cb_w8a8_gemm_noalloc(const int8_t* aq, const float* a_scale, const in
    cb_workspace_status for callers that hold no workspace. */
 CB_API int cb_w8a8_noalloc_status(int* device_status, cb_stream_t stream);
 
+/* ---- FP8 (e4m3) W8A8 GEMM ----------------------------------------------- */
+/* The reference measures its W8A8 path against vLLM's fp8 cutlass_scaled_mm
+   on e4m3 operands (profiling/dense_qwen/bench_l2_boundary.py:54-57, 66-68;
+   profiling/dense_qwen/bench_dense_proj.py:40-43, 113-115). These entry points
+   give that path on the tcgen05 kind::f8f6f4 tensor cores. */
+enum cb_fp8_mode {
+  CB_FP8_PER_TOKEN = 0,          /* dynamic, one scale per (batch, row) */
+  CB_FP8_PER_TENSOR_DYNAMIC = 1, /* dynamic, one scale per batch entry from its amax */
+  CB_FP8_STATIC = 2              /* scale[b * scale_stride_b] given by the caller */
+};
+/* e4m3 quantization of activations a [batch, M, K] (f16 / bf16, K contiguous):
+   dynamic scale = max(amax / 448, 1 / (448 * 512)) (IEEE-rounded division),
+   q = e4m3(clamp(a / scale, -448, 448)), round to nearest even. q: uint8 e4m3
+   bytes [batch, M, K]; scale: fp32, scale[b * scale_stride_b + m] per token or
+   scale[b * scale_stride_b] per tensor. Replaces vllm._custom_ops.scaled_fp8_quant
+   (its per-tensor dynamic, per-token dynamic and static modes). */
+CB_API int cb_quant_act_fp8(const void* a, int a_dtype, int64_t batch, int64_t M, int64_t K, int64_t a_stride_b,
+                            int64_t a_stride_m, uint8_t* q, int64_t q_stride_b, int64_t q_stride_m, float* scale,
+                            int64_t scale_stride_b, int mode, cb_stream_t stream);
+/* out[b, m, n] = cvt( (acc * a_scale) * w_scale (+ bias[n]) ), acc = sum_k aq * w
+   accumulated in fp32 on the tensor cores (e4m3 products are exact in fp32).
+   aq: e4m3 [batch, M, K], w: e4m3 [batch, N, K] (K-major), as cb_w8a8_gemm.
+   a_scale: per token (a_scale[b * s_ab + m]) or, with a_scale_per_tensor, one
+   value per batch entry (a_scale[b * s_ab]); w_scale likewise per channel or
+   per tensor. strides (elements): {aq_b, aq_m, w_b, w_n, out_b, out_m,
+   a_scale_b, w_scale_b}. Workspace: cb_workspace_bytes(CB_OP_W8A8, ...).
+   Replaces vllm._custom_ops.cutlass_scaled_mm on e4m3 operands. */
+CB_API int cb_fp8_gemm(const uint8_t* aq, const float* a_scale, int a_scale_per_tensor, const uint8_t* w,
+                       const float* w_scale, int w_scale_per_tensor, const void* bias, int bias_dtype, void* out,
+                       int out_dtype, int64_t batch, int64_t M, int64_t N, int64_t K, const int64_t* strides,
+                       void* workspace, size_t workspace_bytes, cb_stream_t stream);
+
 /* ---- W4A16 int4 group-dequant GEMM / batched INT4 BMM -------------------- */
 /* out[b, m, n] = sum_k a[b, m, k] * (q[b, k, n] * s[b, k / group_size, n]).
    Replaces kernel_batched_w4a16_simple / batched_int4_gemm

@@ -347,6 +347,34 @@ def e4m3_round(x) -> tuple[np.ndarray, np.ndarray]:
     return bits, v.astype(np.float32)
 
 
+def fp8_quant(x_f32: np.ndarray, scale=None):
+    """e4m3 quantization of activations as vLLM's scaled_fp8_quant (the call of
+    profiling/dense_qwen/bench_l2_boundary.py:54-57): per row of x [..., K] when
+    ``scale`` is None (scale = max(amax / 448, 1 / (448 * 512)), IEEE fp32
+    division), else with the given scale; q = e4m3(clamp(x / scale, +-448)),
+    round to nearest even. Returns (bits uint8 like x, values fp32 like x, scale)."""
+    x = np.asarray(x_f32, dtype=np.float32)
+    if scale is None:
+        amax = np.abs(x).max(axis=-1)
+        scale = np.maximum((amax / np.float32(448.0)).astype(np.float32), np.float32(1.0 / (448.0 * 512.0)))
+        s = scale[..., None]
+    else:
+        scale = np.asarray(scale, dtype=np.float32)
+        s = scale
+    y = np.clip((x / s).astype(np.float32), -448.0, 448.0)
+    bits, mag = e4m3_round(np.abs(y))
+    neg = np.signbit(y)  # the sign survives rounding to zero (-0.0), as the hardware conversion keeps it
+    bits = np.where(neg, bits | 0x80, bits).astype(np.uint8)
+    vals = np.where(neg, -mag, mag).astype(np.float32)
+    return bits, vals, np.asarray(scale, dtype=np.float32)
+
+
+def fp8_gemm(a_vals: np.ndarray, w_vals_nk: np.ndarray) -> np.ndarray:
+    """Exact sum_k a[..., m, k] * w[..., n, k] of e4m3 values (float64: every
+    product of two e4m3 values and their sums at these sizes are exact)."""
+    return np.matmul(np.asarray(a_vals, np.float64), np.swapaxes(np.asarray(w_vals_nk, np.float64), -1, -2))
+
+
 def e4m3_bits_to_f32(b) -> np.ndarray:
     b = np.asarray(b, dtype=np.uint8).astype(np.int64)
     sign = np.where(b & 0x80, -1.0, 1.0)

@@ -148,3 +148,22 @@ def test_nvfp4_gemm_oracle_is_dequant_matmul():
     assert np.array_equal(out, ref)
     # dequantized values approximate x * gs (fp4 relative error < 1/3 per element, scale rounding aside)
     assert np.abs(O.nvfp4_dequant(ap, asf) - a * 2.0).max() <= 0.5 * np.abs(a * 2.0).max()
+
+
+def test_fp8_oracle_pinned_to_torch_e4m3():
+    """oracle.fp8_quant's e4m3 rounding (round to nearest even, saturate at 448,
+    sign kept on values that round to zero) equals torch's float8_e4m3fn
+    conversion on the CPU, and the per-token scale is max(amax / 448, 1 / (448 * 512))."""
+    import torch
+    rng = np.random.default_rng(17)
+    x = (rng.standard_normal((7, 513)) * np.exp(rng.uniform(-12, 8, (7, 1)))).astype(np.float32)
+    x[0, :8] = [-1e-9, 1e-9, -0.0, 0.0, 1e6, -1e6, 896.0, -3e-5]
+    x[1] = 0.0
+    bits, vals, scale = O.fp8_quant(x)
+    amax = np.abs(x).max(axis=1)
+    assert np.array_equal(scale, np.maximum((amax / np.float32(448)).astype(np.float32), np.float32(1 / (448 * 512))))
+    y = np.clip((x / scale[:, None]).astype(np.float32), -448, 448)
+    t = torch.from_numpy(y).to(torch.float8_e4m3fn)
+    assert np.array_equal(t.view(torch.uint8).numpy(), bits)
+    assert np.array_equal(t.float().numpy(), vals)
+    assert np.array_equal(O.e4m3_bits_to_f32(bits), vals)
