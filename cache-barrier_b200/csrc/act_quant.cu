@@ -102,6 +102,33 @@ __global__ void __launch_bounds__(kThreads) act_quant_kernel(const T* __restrict
   if (threadIdx.x == 0) scale[b * s_sb + m] = s;
 }
 
+// Short rows (K <= kWarpRowMaxK), many of them (a batch of heads x tokens): one
+// warp per row, kThreads / 32 rows per CTA, the same arithmetic as
+// act_quant_kernel. A CTA per row would spend its time launching.
+constexpr int kWarpRowMaxK = 2048;
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) act_quant_rows_kernel(const T* __restrict__ a, long long a_sb,
+                                                                   long long a_sm, int8_t* __restrict__ q,
+                                                                   long long q_sb, long long q_sm,
+                                                                   float* __restrict__ scale, long long s_sb, int M,
+                                                                   int K, long long rows) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const int lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const long long b = row / M, m = row % M;
+  const T* ar = a + b * a_sb + m * a_sm;
+  int8_t* qr = q + b * q_sb + m * q_sm;
+  float amax = 0.0f;
+  for (int i = lane; i < K; i += 32) amax = fmaxf(amax, fabsf(to_f32(ar[i])));
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-8f);
+  for (int i = lane; i < K; i += 32) qr[i] = quant1(to_f32(ar[i]), s);
+  if (lane == 0) scale[b * s_sb + m] = s;
+}
+
 // ---------------------------------------------------------------------------
 // e4m3 fp8 activations (the operands of the fp8 W8A8 GEMM), in the three modes
 // of vLLM's scaled_fp8_quant, the call the reference's dense harnesses make
@@ -257,6 +284,22 @@ int launch_act_quant(const void* a, int a_dtype, int64_t batch, int64_t M, int64
   cfg.numAttrs = 1;
   const int Mi = static_cast<int>(M), Ki = static_cast<int>(K);
   cudaError_t e;
+  if (K <= kWarpRowMaxK && rows >= 64) {
+    cfg.gridDim = dim3(static_cast<unsigned>((rows + kThreads / 32 - 1) / (kThreads / 32)));
+    if (a_dtype == CB_DTYPE_BF16)
+      e = cudaLaunchKernelEx(&cfg, act_quant_rows_kernel<__nv_bfloat16>, static_cast<const __nv_bfloat16*>(a),
+                             static_cast<long long>(a_sb), static_cast<long long>(a_sm), q,
+                             static_cast<long long>(q_sb), static_cast<long long>(q_sm), scale,
+                             static_cast<long long>(s_sb), Mi, Ki, rows);
+    else if (a_dtype == CB_DTYPE_F16)
+      e = cudaLaunchKernelEx(&cfg, act_quant_rows_kernel<__half>, static_cast<const __half*>(a),
+                             static_cast<long long>(a_sb), static_cast<long long>(a_sm), q,
+                             static_cast<long long>(q_sb), static_cast<long long>(q_sm), scale,
+                             static_cast<long long>(s_sb), Mi, Ki, rows);
+    else
+      return CB_ERR_DTYPE;
+    return cuda_status(e);
+  }
   if (a_dtype == CB_DTYPE_BF16) {
     e = cudaLaunchKernelEx(&cfg, act_quant_kernel<__nv_bfloat16>, static_cast<const __nv_bfloat16*>(a),
                            static_cast<long long>(a_sb), static_cast<long long>(a_sm), q, static_cast<long long>(q_sb),

@@ -41,6 +41,23 @@ constexpr int kThreads = 224;
 constexpr int kWaiterWarp = 6;
 constexpr int kHandoffBar = 2;  // named barrier: MMA warp + stage waiter (barrier 1 is the epilogue's)
 constexpr uint32_t kWTileBytes = kBlockN * kBlockK;
+// Fewest k-blocks a CTA takes when the problem has fewer k-blocks than that
+// many per SM: small GEMMs then run on fewer CTAs instead of cutting each tile
+// into many one-k-block partials that one collector must sum.
+constexpr int kMinKbPerCta = 8;
+// Segments (tiles) whose scales the epilogue has in flight: they are copied
+// into shared memory (cp.async) kScaleRing - 1 segments ahead, so a short
+// segment (one k-block) does not wait a memory round trip for its scales.
+constexpr int kScaleRing = 4;
+
+__device__ __forceinline__ void cp_async_f32(float* dst, const float* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // Operand kinds: signed int8 (W8A8), unsigned 8-bit (the W4A4 reference-wrap
 // mode), both with int32 accumulators; e4m3 fp8 with fp32 accumulators. All are
@@ -237,15 +254,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   using Acc = typename AccOf<KIND>::T;
   constexpr uint32_t kATileBytes = TN * kBlockK;
   constexpr uint32_t kStageBytes = kWTileBytes + kATileBytes;
-  constexpr uint32_t kTmemCols = TN < 32 ? 32 : TN;
+  constexpr uint32_t kAccCols = TN < 32 ? 32 : TN;
+  constexpr uint32_t kTmemCols = 2 * kAccCols;  // two accumulators: a tile's MMAs overlap the previous tile's epilogue
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
-  __shared__ __align__(8) uint64_t tfull_bar, tempty_bar, drain_bar;
+  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ int sh_issued, sh_consumed, sh_is_last;
+  // scales of the next kScaleRing segments (epilogue, token tiles up to 32)
+  __shared__ float ws_ring[kScaleRing][kBlockN];
+  __shared__ float as_ring[kScaleRing][TN <= 32 ? TN : 1];
   volatile int* abort_ptr = &abort_flag;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -269,8 +290,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&tfull_bar, 1);
-    mbar_init(&tempty_bar, 4);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 4);
+    }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
     sh_issued = 0;
@@ -353,20 +376,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                            : KIND == kKindE4M3 ? idesc_e4m3_f32(kBlockN, TN)
                                                : idesc_i8_s32(kBlockN, TN);
     int stage = 0;
-    uint32_t acc_phase = 0;
     int consumed = 0;
     int n_tfull = 0;
     bool bad = false;
     long long g = g0;
     int kb_first = static_cast<int>(g0 % KB);
-    while (g < g1) {
+    for (int seg = 0; g < g1; ++seg) {
       const long long seg_len = (KB - kb_first) < (g1 - g) ? (KB - kb_first) : (g1 - g);
       const long long seg_end = g + seg_len;
       kb_first = 0;
-      // The epilogue must have drained the accumulator of the previous segment.
-      if (lane == 0) bad = !mbar_wait(&tempty_bar, acc_phase ^ 1u, abort_ptr, p.status);
+      // Segment seg accumulates into accumulator seg % 2, free once the epilogue
+      // drained the segment two back.
+      const int acc = seg & 1;
+      const uint32_t tmem_acc = tmem_d + acc * kAccCols;
+      if (lane == 0 && !bad)
+        bad = !mbar_wait(&tempty_bar[acc], static_cast<uint32_t>(((seg >> 1) & 1) ^ 1), abort_ptr, p.status);
       bad = __shfl_sync(0xffffffffu, bad, 0);
-      acc_phase ^= 1u;
       bool stop = false;
       for (bool first = true; g < seg_end; ++g, first = false) {
         if (named_bar_or(kHandoffBar, 64, bad)) {
@@ -380,10 +405,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBlockK / 32; ++kk) {
             if constexpr (KIND == kKindE4M3)
-              mma_f8_ss(tmem_d, smem_desc_sw128(wa + kk * 32), smem_desc_sw128(aa + kk * 32), idesc,
+              mma_f8_ss(tmem_acc, smem_desc_sw128(wa + kk * 32), smem_desc_sw128(aa + kk * 32), idesc,
                         (first && kk == 0) ? 0u : 1u);
             else
-              mma_i8_ss(tmem_d, smem_desc_sw128(wa + kk * 32), smem_desc_sw128(aa + kk * 32), idesc,
+              mma_i8_ss(tmem_acc, smem_desc_sw128(wa + kk * 32), smem_desc_sw128(aa + kk * 32), idesc,
                         (first && kk == 0) ? 0u : 1u);
           }
           mma_commit(&empty_bar[stage]);
@@ -393,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++stage == S) stage = 0;
       }
       if (stop) break;
-      if (lane == 0) mma_commit(&tfull_bar);
+      if (lane == 0) mma_commit(&tfull_bar[acc]);
       __syncwarp();
       ++n_tfull;
     }
@@ -412,8 +437,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
       const int j = consumed - 1 - lane;  // lane l waits the (l+1)-th most recent stage release
       if (lane < S && j >= 0) mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
-      if (lane == 31 && n_tfull > 0)
-        mbar_wait(&tfull_bar, static_cast<uint32_t>((n_tfull - 1) & 1), nullptr, p.status);
+      const int t = n_tfull - 1 - (lane - 30);  // lanes 30, 31: the last two accumulator hand-offs
+      if (lane >= 30 && t >= 0) mbar_wait(&tfull_bar[t & 1], static_cast<uint32_t>((t >> 1) & 1), nullptr, p.status);
     }
     __syncwarp();
   } else if (warp == kWaiterWarp) {
@@ -446,11 +471,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait_counter(p.status + 1, 1, abort_ptr, p.status, p.dbg_wait_ns);
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const uint32_t lane_addr = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
-    uint32_t acc_phase = 0;
+    const uint32_t lane_addr0 = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
+    int seg = 0;
     long long g = g0;
     long long tile = g0 / KB;
     int kb0 = static_cast<int>(g0 - tile * KB);
+    constexpr bool kPrefetch = TN <= 32;
+    const long long last_tile = (g1 - 1) / KB;
+    // Copies (cp.async, one commit group per segment) of segment t's scales into
+    // ring slot t % kScaleRing: each thread its row's w_scale, threads 0..TN-1
+    // one a_scale each.
+    auto issue_scales = [&](long long t, int slot) {
+      if (t <= last_tile && !p.raw_f32) {
+        int hh, nnt, mmt;
+        decode_tile(p, t, hh, nnt, mmt);
+        const int nn = nnt * kBlockN + row;
+        if (nn < p.N) cp_async_f32(&ws_ring[slot][row], p.w_scale + hh * p.ws_sb + nn * p.ws_sn);
+        const int mm = mmt * TN + row;
+        if (row < TN && mm < p.M) cp_async_f32(&as_ring[slot][row], p.a_scale + hh * p.as_sb + mm * p.as_sm);
+      }
+      cp_async_commit();
+    };
+    if constexpr (kPrefetch) {
+#pragma unroll
+      for (int d = 0; d < kScaleRing - 1; ++d) issue_scales(tile + d, d);
+    }
     for (; g < g1; ++tile, kb0 = 0) {
       const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
       const int kb1 = kb0 + static_cast<int>(seg_len);
@@ -460,29 +505,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int c_first = whole ? 0 : p.sk.owner(tile * KB);
       const int c_last = whole ? 0 : p.sk.owner((tile + 1) * KB - 1);
       const bool collect = !whole && static_cast<int>(blockIdx.x) == c_first;
-      constexpr bool kPrefetch = TN <= 32;
       int h, nt, mt;
       decode_tile(p, tile, h, nt, mt);
       const int n = nt * kBlockN + row;
       const int m0 = mt * TN;
-      // Scales of the rows this segment stores, loaded before any wait so the
-      // stores after the last MMA depend on nothing in flight.
+      // Scales of the rows this segment stores: copied into the ring
+      // kScaleRing - 1 segments ago; wait for this segment's group, make every
+      // thread's copies visible, then reuse the slot the previous segment read.
       float ws_pre = 1.0f;
       float bias_pre = 0.0f;
       float as_pre[kPrefetch ? TN : 1];
       if constexpr (kPrefetch) {
-        const bool stores = whole || collect;
+        const int slot = seg % kScaleRing;
+        cp_async_wait<kScaleRing - 2>();
+        named_bar_sync(1, 128);
+        issue_scales(tile + kScaleRing - 1, (seg + kScaleRing - 1) % kScaleRing);
+        if (!p.raw_f32) {
 #pragma unroll
-        for (int j = 0; j < TN; ++j)
-          as_pre[j] = (stores && !p.raw_f32 && m0 + j < p.M) ? __ldg(p.a_scale + h * p.as_sb + (m0 + j) * p.as_sm) : 1.0f;
-        if (stores && !p.raw_f32 && n < p.N) ws_pre = __ldg(p.w_scale + h * p.ws_sb + n * p.ws_sn);
-        if (stores && p.bias && n < p.N) bias_pre = load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n);
-        // Consume the values here, so the compiler cannot sink the loads to
-        // their use after the last MMA.
+          for (int j = 0; j < TN; ++j) as_pre[j] = m0 + j < p.M ? as_ring[slot][j] : 1.0f;
+          if (n < p.N) ws_pre = ws_ring[slot][row];
+        } else {
 #pragma unroll
-        for (int j = 0; j < TN; ++j) asm volatile("" ::"f"(as_pre[j]));
-        asm volatile("" ::"f"(ws_pre));
-        asm volatile("" ::"f"(bias_pre));
+          for (int j = 0; j < TN; ++j) as_pre[j] = 1.0f;
+        }
+        if ((whole || collect) && p.bias && n < p.N) bias_pre = load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n);
       }
       Acc other[kPrefetch ? TN : 1];
       bool others_ready = true;
@@ -513,8 +559,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < TN; ++j) keep(other[j]);
         }
       }
-      const bool got = mbar_wait(&tfull_bar, acc_phase, abort_ptr, p.status);
-      acc_phase ^= 1u;
+      const int acc = seg & 1;
+      const uint32_t lane_addr = lane_addr0 + acc * kAccCols;
+      const bool got = mbar_wait(&tfull_bar[acc], static_cast<uint32_t>((seg >> 1) & 1), abort_ptr, p.status);
+      ++seg;
       const bool live = __all_sync(0xffffffffu, got);
       tc_fence_after();
       if (whole) {
@@ -560,7 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar);
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       } else if (!collect) {
         // Partial tile, not its first contributor: publish this CTA's part
         // (this is the CTA's first segment, long before the collector needs it).
@@ -579,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar);
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
         __threadfence();
         named_bar_sync(1, 128);
         if (threadIdx.x == 64 && !*abort_ptr) atomicAdd(&p.counters[c_first], 1);
@@ -629,11 +677,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar);
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       }
     }
   }
 
+  cp_async_wait<0>();  // no scale copy outlives the CTA (the epilogue consumed all of them)
   __syncthreads();
   if (warp == 0) {
     if (lane == 0 && abort_flag) {
@@ -729,7 +778,7 @@ int launch_w8a8(const W8A8Launch& L, cudaStream_t stream) {
   const long long total = tiles * p.kb_per_tile;
   int sms = sm_count();
   if (sms <= 0) return CB_ERR_CUDA;
-  const int grid = stream_k_grid(total, sms, TN);
+  const int grid = stream_k_grid(total, sms, TN, kMinKbPerCta);
   const size_t need = workspace_need(grid, static_cast<size_t>(TN) * kBlockN * sizeof(int32_t));
   if (L.workspace == nullptr || L.workspace_bytes < need) return CB_ERR_WORKSPACE;
   // Ring depth: as many stages as ~200 KiB of shared memory holds.
