@@ -43,12 +43,15 @@ constexpr int kHandoffBar = 2;  // named barrier: MMA warp + stage waiter (barri
 constexpr uint32_t kWTileBytes = kBlockN * kBlockK;
 // Fewest k-blocks a CTA takes when the problem has fewer k-blocks than that
 // many per SM: small GEMMs then run on fewer CTAs instead of cutting each tile
-// into many one-k-block partials that one collector must sum.
+// into many one-k-block partials that one CTA must sum.
 constexpr int kMinKbPerCta = 8;
 // Segments (tiles) whose scales the epilogue has in flight: they are copied
 // into shared memory (cp.async) kScaleRing - 1 segments ahead, so a short
 // segment (one k-block) does not wait a memory round trip for its scales.
 constexpr int kScaleRing = 4;
+// How long the first contributor of a cut tile polls for the other
+// contributors' parts before publishing its own instead (last-arriver fallback).
+constexpr unsigned long long kFirstPollNs = 10000;
 
 __device__ __forceinline__ void cp_async_f32(float* dst, const float* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -171,7 +174,7 @@ __device__ __forceinline__ void emit_row_pre(const Params& p, int h, int n, int 
 // emit_row_pre for 16-bit outputs through shared memory: the warp stages its
 // 32 columns x 16 tokens (thread = column) and stores them back as 16-byte
 // vectors of 8 columns, one eighth of the store instructions of the
-// column-per-thread form. Those stores set the kernel's tail: the collector's
+// column-per-thread form. Those stores set the kernel's tail: the reducing CTA's
 // sum-and-store after its last MMA took ~1 / 1.8 / 3.3 us at T = 1 / 16 / 32.
 // Same arithmetic and rounding as emit_row_pre.
 template <int OUT_BF16, typename Acc>
@@ -298,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     abort_flag = 0;
     sh_issued = 0;
     sh_consumed = 0;
-    sh_is_last = 0;  // collector: whether every other contributor has published
+    sh_is_last = 0;  // cut tiles: whether this CTA is the last contributor
     fence_mbar_init();
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_a);
@@ -499,12 +502,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (; g < g1; ++tile, kb0 = 0) {
       const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
       const int kb1 = kb0 + static_cast<int>(seg_len);
-      const bool first_seg = (g == g0);
       g += seg_len;
       const bool whole = (kb0 == 0 && kb1 == KB);
       const int c_first = whole ? 0 : p.sk.owner(tile * KB);
       const int c_last = whole ? 0 : p.sk.owner((tile + 1) * KB - 1);
-      const bool collect = !whole && static_cast<int>(blockIdx.x) == c_first;
       int h, nt, mt;
       decode_tile(p, tile, h, nt, mt);
       const int n = nt * kBlockN + row;
@@ -528,21 +529,42 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < TN; ++j) as_pre[j] = 1.0f;
         }
-        if ((whole || collect) && p.bias && n < p.N) bias_pre = load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n);
+        if (p.bias && n < p.N) bias_pre = load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n);
       }
+      // Cut tile: last-arriver reduction. Every contributor publishes its part
+      // and bumps the tile's counter; the one that arrives last sums the parts
+      // in a fixed order (the first contributor's part + the left fold of the
+      // others in CTA order, so fp32 results do not depend on who is last) and
+      // stores the tile. Nobody waits for another CTA. A contributor that already
+      // sees every other part published is last without publishing its own; the
+      // first contributor then pulls the others' parts in while its last MMAs run.
+      const int n_contrib = c_last - c_first + 1;
+      const bool is_first = static_cast<int>(blockIdx.x) == c_first;
+      bool last = false;
       Acc other[kPrefetch ? TN : 1];
-      bool others_ready = true;
-      if (collect) {
-        // The other contributors handled this tile at the start of their ranges;
-        // wait (bounded) for all of them, then pull their parts in while this
-        // CTA's own last MMAs are still running.
-        if (threadIdx.x == 64) sh_is_last = wait_counter(&p.counters[c_first], c_last - c_first, abort_ptr, p.status);
+      if (!whole) {
+        // The first contributor (whose range ends in this tile; the others
+        // covered it at the start of theirs) polls for their parts for at most
+        // kFirstPollNs: co-resident contributors are done by then, and this CTA
+        // then reduces without publishing. If they are not (some CTAs were not
+        // resident), it publishes its part and the last arriver finishes the
+        // tile: slower, never stuck. The others only look once.
+        if (threadIdx.x == 64) {
+          const int* ctr = &p.counters[c_first];
+          bool done = ld_acquire_gpu(ctr) == n_contrib - 1;
+          if (is_first && !done) {
+            const unsigned long long t0 = global_timer_ns();
+            while (!done && !*abort_ptr && global_timer_ns() - t0 < kFirstPollNs) {
+              __nanosleep(64);
+              done = ld_acquire_gpu(ctr) == n_contrib - 1;
+            }
+          }
+          sh_is_last = done ? 1 : 0;
+        }
         named_bar_sync(1, 128);
-        others_ready = sh_is_last != 0;
+        last = sh_is_last != 0;
         if constexpr (kPrefetch) {
-#pragma unroll
-          for (int j = 0; j < TN; ++j) other[j] = Acc(0);
-          if (others_ready) {
+          if (last && is_first) {
 #pragma unroll
             for (int c = 0; c < TN / 16; ++c) {
               Acc v[16];
@@ -552,11 +574,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) other[c * 16 + j] = v[j];
             }
-          }
-          // Complete the partial sums now, while this CTA's last MMAs run; the
-          // compiler would otherwise sink the loads to their use after the wait.
+            // complete the loads now, while this CTA's last MMAs run
 #pragma unroll
-          for (int j = 0; j < TN; ++j) keep(other[j]);
+            for (int j = 0; j < TN; ++j) keep(other[j]);
+          }
         }
       }
       const int acc = seg & 1;
@@ -609,46 +630,82 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-      } else if (!collect) {
-        // Partial tile, not its first contributor: publish this CTA's part
-        // (this is the CTA's first segment, long before the collector needs it).
-        const int slot = blockIdx.x * 2 + (first_seg ? 0 : 1);
-        uint32_t* dst = static_cast<uint32_t*>(p.partials) + static_cast<long long>(slot) * TN * kBlockN;
-        if (live) {
-#pragma unroll 1
-          for (int c = 0; c < TN / 16; ++c) {
-            uint32_t r[16];
-            __syncwarp();
-            tmem_ld16(lane_addr + c * 16, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) dst[(c * 16 + j) * kBlockN + row] = r[j];  // raw accumulator bits
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (threadIdx.x == 64 && !*abort_ptr) atomicAdd(&p.counters[c_first], 1);
       } else {
-        // Partial tile, first contributor (its last segment): the collector adds
-        // its own accumulator to the others' published parts and stores the tile.
-        if (live && others_ready) {
-          if constexpr (kPrefetch) {
-#pragma unroll
+        const bool prefetched = kPrefetch && last && is_first;
+        if (!last) {
+          // publish this CTA's part (raw accumulator bits) and count it
+          const int slot = static_cast<int>(blockIdx.x) * 2 + p.sk.kind(blockIdx.x, tile);
+          uint32_t* dst = static_cast<uint32_t*>(p.partials) + static_cast<long long>(slot) * TN * kBlockN;
+          if (live) {
+#pragma unroll 1
             for (int c = 0; c < TN / 16; ++c) {
               uint32_t r[16];
               __syncwarp();
               tmem_ld16(lane_addr + c * 16, r);
               tmem_ld_wait();
-              Acc v[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) dst[(c * 16 + j) * kBlockN + row] = r[j];
+            }
+          }
+          __threadfence();
+          named_bar_sync(1, 128);
+          if (threadIdx.x == 64)
+            sh_is_last = (!*abort_ptr && atomicAdd(&p.counters[c_first], 1) == n_contrib - 1) ? 1 : 0;
+          named_bar_sync(1, 128);
+          last = sh_is_last != 0;
+          if (last) __threadfence();
+        }
+        if (last && live) {
+          // part of contributor cc, chunk c of this thread's row
+          auto part = [&](int cc, int c, Acc (&v)[16]) {
+            const int slot = cc * 2 + p.sk.kind(cc, tile);
+            const Acc* src = static_cast<const Acc*>(p.partials) + static_cast<long long>(slot) * TN * kBlockN +
+                             (c * 16) * kBlockN + row;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = __ldcg(src + j * kBlockN);
+          };
+#pragma unroll(kPrefetch ? 2 : 1)
+          for (int c = 0; c < TN / 16; ++c) {
+            uint32_t r[16];
+            __syncwarp();
+            tmem_ld16(lane_addr + c * 16, r);
+            tmem_ld_wait();
+            Acc own[16], v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) own[j] = acc_from_bits<Acc>(r[j]);
+            // S = left fold of the parts of c_first + 1 .. c_last
+            if (prefetched) {
+              if constexpr (kPrefetch) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = other[c * 16 + j];
+              }
+            } else {
+              for (int cc = c_first + 1; cc <= c_last; ++cc) {
+                Acc w[16];
+                if (cc == static_cast<int>(blockIdx.x)) {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) w[j] = own[j];
+                } else {
+                  part(cc, c, w);
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = cc == c_first + 1 ? w[j] : v[j] + w[j];
+              }
+            }
+            // + the first contributor's part
+            Acc pf[16];
+            if (is_first) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) pf[j] = own[j];
+            } else {
+              part(c_first, c, pf);
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = pf[j] + v[j];
+            if constexpr (kPrefetch) {
               float as16[16];
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                v[j] = acc_from_bits<Acc>(r[j]) + other[c * 16 + j];
-                as16[j] = as_pre[c * 16 + j];
-              }
+              for (int j = 0; j < 16; ++j) as16[j] = as_pre[c * 16 + j];
               if (p.vec_out) {
                 uint16_t* stg = epi_stage + (warp - 2) * 512;
                 if (p.out_dtype == CB_DTYPE_BF16)
@@ -658,18 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               } else {
                 emit_row_pre<Acc>(p, h, n, m0, c * 16, v, ws_pre, bias_pre, as16);
               }
-            }
-          } else {
-#pragma unroll 1
-            for (int c = 0; c < TN / 16; ++c) {
-              uint32_t r[16];
-              __syncwarp();
-              tmem_ld16(lane_addr + c * 16, r);
-              tmem_ld_wait();
-              Acc v[16];
-#pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] = acc_from_bits<Acc>(r[j]);
-              sum_published<TN, Acc>(p, c_first + 1, c_last, c, row, v);
+            } else {
               emit_row_any<TN, Acc>(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - 2) * 512);
             }
           }
