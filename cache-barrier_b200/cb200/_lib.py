@@ -75,6 +75,7 @@ SIGNATURES = {
     "cb_w8a8_gemm_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "cb_w8a8_noalloc_status": (_int, [ctypes.POINTER(_int), _vp]),
     "cb_debug_force_wait_timeout": (None, [ctypes.c_uint64]),
+    "cb_debug_force_last_arriver": (None, [ctypes.c_int]),
     "cb_w8a8_gemm_dynamic": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _vp, _vp,
                                     _sz, _vp]),
     "cb_w4a16_gemm": (_int, [_vp, _int, _vp, _vp, _int, _i64, _vp, _int, _i64, _i64, _i64, _i64, _vp, _vp, _sz,

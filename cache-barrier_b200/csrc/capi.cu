@@ -14,9 +14,11 @@ namespace cb {
 
 namespace {
 std::atomic<unsigned long long> g_debug_wait_ns{0};
+std::atomic<bool> g_force_last_arriver{false};
 }  // namespace
 
 unsigned long long debug_wait_ns() { return g_debug_wait_ns.load(std::memory_order_relaxed); }
+bool debug_force_last_arriver() { return g_force_last_arriver.load(std::memory_order_relaxed); }
 
 int sm_count() {
   static int cached[64] = {0};
@@ -292,6 +294,8 @@ int cb_workspace_status(void* workspace, int* device_status, cb_stream_t stream)
 void cb_debug_force_wait_timeout(uint64_t limit_ns) {
   g_debug_wait_ns.store(static_cast<unsigned long long>(limit_ns), std::memory_order_relaxed);
 }
+
+void cb_debug_force_last_arriver(int on) { g_force_last_arriver.store(on != 0, std::memory_order_relaxed); }
 
 int cb_quant_act_i8(const void* a, int a_dtype, int64_t batch, int64_t M, int64_t K, int64_t a_stride_b,
                     int64_t a_stride_m, int8_t* q, int64_t q_stride_b, int64_t q_stride_m, float* scale,

@@ -18,10 +18,20 @@
 
 namespace cb {
 
+// How long the first contributor of a cut tile polls for the other
+// contributors' parts before it publishes its own part instead. Contributors
+// that are resident together finish well inside it; when some are not (another
+// kernel holds SMs), the last one to arrive reduces the tile, so no CTA ever
+// waits on one that may not be running.
+constexpr unsigned long long kFirstPollNs = 10000;
+
 struct StreamK {
   long long total;  // tiles * kb_per_tile
   int grid;         // number of CTAs
   int kb_per_tile;
+  // first contributor's poll limit: kFirstPollNs, or 0 under the test hook
+  // that forces the last-arriver path (cb_debug_force_last_arriver)
+  unsigned long long first_poll_ns;
 
   __host__ __device__ long long start(int c) const { return static_cast<long long>(c) * total / grid; }
   // CTA whose range holds global k-block g.

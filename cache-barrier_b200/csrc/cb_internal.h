@@ -19,6 +19,9 @@ constexpr size_t kWsHeader = 256;
 // Wait limit of the failure-detection test hook (0 = off), set by
 // cb_debug_force_wait_timeout and read by the W8A8 launcher.
 unsigned long long debug_wait_ns();
+// Split-K test hook (cb_debug_force_last_arriver): cut tiles skip the first
+// contributor's poll, so every one is reduced by its last arriver.
+bool debug_force_last_arriver();
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 

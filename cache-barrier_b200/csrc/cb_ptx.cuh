@@ -109,6 +109,20 @@ __device__ __forceinline__ bool wait_counter(const int* ctr, int target, volatil
   }
 }
 
+// Short bounded poll until *ctr == target. Expiry is not an error: the caller
+// has a way on that does not depend on the other CTAs (the split-K kernels'
+// last-arriver fallback).
+__device__ __forceinline__ bool poll_counter(const int* ctr, int target, volatile int* abort_flag,
+                                             unsigned long long limit_ns) {
+  if (ld_acquire_gpu(ctr) == target) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (!(abort_flag && *abort_flag) && global_timer_ns() - t0 < limit_ns) {
+    __nanosleep(64);
+    if (ld_acquire_gpu(ctr) == target) return true;
+  }
+  return false;
+}
+
 // ----------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), single-CTA destination, completion on an mbarrier.
 // ----------------------------------------------------------------------------

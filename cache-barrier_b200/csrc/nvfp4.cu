@@ -477,46 +477,63 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (; g < g1; ++tile, kb0 = 0) {
       const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
       const int kb1 = kb0 + static_cast<int>(seg_len);
-      const bool first_seg = (g == g0);
       g += seg_len;
       const bool whole = (kb0 == 0 && kb1 == KB);
       const int c_first = whole ? 0 : p.sk.owner(tile * KB);
       const int c_last = whole ? 0 : p.sk.owner((tile + 1) * KB - 1);
-      const bool collect = !whole && static_cast<int>(blockIdx.x) == c_first;
+      const int n_contrib = c_last - c_first + 1;
+      const bool is_first = static_cast<int>(blockIdx.x) == c_first;
       int nt, mt;
       decode_tile(p, tile, nt, mt);
       const int n = nt * kBlockN + row;
       const int m0 = mt * TN;
-      bool others_ready = true;
-      // The collector sums the other contributors' parts (in CTA order) while
-      // its own last MMAs still run, then adds its accumulator.
+      // Cut tile: the first contributor polls for the others' parts for at most
+      // kFirstPollNs and then reduces without publishing, pulling the parts in
+      // while its own last MMAs run; otherwise every contributor publishes and
+      // the last to arrive reduces. Either way the sum is the first
+      // contributor's part + the left fold of the others in CTA order.
       constexpr bool kPrefetch = TN <= 32;
       float other[kPrefetch ? TN : 1];
-      if (collect) {
-        if (threadIdx.x == 64) sh_is_last = wait_counter(&p.counters[c_first], c_last - c_first, abort_ptr, p.status);
+      bool last = false;
+      if (!whole) {
+        if (threadIdx.x == 64)
+          sh_is_last = poll_counter(&p.counters[c_first], n_contrib - 1, abort_ptr, is_first ? p.sk.first_poll_ns : 0) ? 1 : 0;
         named_bar_sync(1, 128);
-        others_ready = sh_is_last != 0;
+        last = sh_is_last != 0;
         if constexpr (kPrefetch) {
+          if (last && is_first) {
 #pragma unroll
-          for (int c = 0; c < TN / 16; ++c) {
-            float t[16];
+            for (int c = 0; c < TN / 16; ++c) {
+              float t[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) t[j] = 0.0f;
-            if (others_ready) sum_published<TN>(p, c_first + 1, c_last, c, row, t);
+              for (int j = 0; j < 16; ++j) t[j] = 0.0f;
+              sum_published<TN>(p, c_first + 1, c_last, c, row, t);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) other[c * 16 + j] = t[j];
+              for (int j = 0; j < 16; ++j) other[c * 16 + j] = t[j];
+            }
+            // Complete the loads now, not at their use after the accumulator wait.
+#pragma unroll
+            for (int j = 0; j < TN; ++j) asm volatile("" ::"f"(other[j]));
           }
-          // Complete the loads now, not at their use after the accumulator wait.
-#pragma unroll
-          for (int j = 0; j < TN; ++j) asm volatile("" ::"f"(other[j]));
         }
       }
       const bool got = mbar_wait(&tfull_bar, acc_phase, abort_ptr, p.status);
       acc_phase ^= 1u;
       const bool live = __all_sync(0xffffffffu, got);
       tc_fence_after();
-      if (whole || collect) {
-        if (live && others_ready) {
+      auto emit = [&](int c, const float (&v)[16]) {
+        if (p.vec_out) {
+          uint16_t* stg = epi_stage + (warp - 2) * 512;
+          if (p.out_dtype == CB_DTYPE_BF16)
+            emit_chunk_vec<1>(p, n - lane, lane, m0, c * 16, v, alpha, stg);
+          else
+            emit_chunk_vec<0>(p, n - lane, lane, m0, c * 16, v, alpha, stg);
+        } else {
+          emit_row(p, n, m0, c * 16, v, alpha);
+        }
+      };
+      if (whole) {
+        if (live) {
 #pragma unroll
           for (int c = 0; c < TN / 16; ++c) {
             uint32_t r[16];
@@ -526,51 +543,86 @@ __global__ void __launch_bounds__(kThreads, 1)
             float v[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-            if (collect) {
-              if constexpr (kPrefetch) {
+            emit(c, v);
+          }
+        }
+      } else {
+        const bool prefetched = kPrefetch && last && is_first;
+        if (!last) {
+          // Publish this CTA's part and count it.
+          const int slot = static_cast<int>(blockIdx.x) * 2 + p.sk.kind(blockIdx.x, tile);
+          float* dst = p.partials + static_cast<long long>(slot) * TN * kBlockN;
+          if (live) {
+#pragma unroll 1
+            for (int c = 0; c < TN / 16; ++c) {
+              uint32_t r[16];
+              __syncwarp();
+              tmem_ld16(lane_addr + c * 16, r);
+              tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], other[c * 16 + j]);
-              } else {
-                sum_published<TN>(p, c_first + 1, c_last, c, row, v);
-              }
-            }
-            if (p.vec_out) {
-              uint16_t* stg = epi_stage + (warp - 2) * 512;
-              if (p.out_dtype == CB_DTYPE_BF16)
-                emit_chunk_vec<1>(p, n - lane, lane, m0, c * 16, v, alpha, stg);
-              else
-                emit_chunk_vec<0>(p, n - lane, lane, m0, c * 16, v, alpha, stg);
-            } else {
-              emit_row(p, n, m0, c * 16, v, alpha);
+              for (int j = 0; j < 16; ++j) dst[(c * 16 + j) * kBlockN + row] = __uint_as_float(r[j]);
             }
           }
-          if (collect && threadIdx.x == 64) p.counters[c_first] = 0;  // next launch starts from zero
+          __threadfence();
+          named_bar_sync(1, 128);
+          if (threadIdx.x == 64)
+            sh_is_last = (!*abort_ptr && atomicAdd(&p.counters[c_first], 1) == n_contrib - 1) ? 1 : 0;
+          named_bar_sync(1, 128);
+          last = sh_is_last != 0;
+          if (last) __threadfence();
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar);
-      } else {
-        // Partial tile, not its first contributor: publish this CTA's part.
-        const int slot = blockIdx.x * 2 + (first_seg ? 0 : 1);
-        float* dst = p.partials + static_cast<long long>(slot) * TN * kBlockN;
-        if (live) {
-#pragma unroll 1
+        if (last && live) {
+          // part of contributor cc, chunk c of this thread's row
+          auto part = [&](int cc, int c, float (&v)[16]) {
+            const int slot = cc * 2 + p.sk.kind(cc, tile);
+            const float* src = p.partials + static_cast<long long>(slot) * TN * kBlockN + (c * 16) * kBlockN + row;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = __ldcg(src + j * kBlockN);
+          };
+#pragma unroll(kPrefetch ? 2 : 1)
           for (int c = 0; c < TN / 16; ++c) {
             uint32_t r[16];
             __syncwarp();
             tmem_ld16(lane_addr + c * 16, r);
             tmem_ld_wait();
+            float own[16], v[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) dst[(c * 16 + j) * kBlockN + row] = __uint_as_float(r[j]);
+            for (int j = 0; j < 16; ++j) own[j] = __uint_as_float(r[j]);
+            if (prefetched) {
+              if constexpr (kPrefetch) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = other[c * 16 + j];
+              }
+            } else {
+              for (int cc = c_first + 1; cc <= c_last; ++cc) {
+                float w[16];
+                if (cc == static_cast<int>(blockIdx.x)) {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) w[j] = own[j];
+                } else {
+                  part(cc, c, w);
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = cc == c_first + 1 ? w[j] : __fadd_rn(v[j], w[j]);
+              }
+            }
+            float pf[16];
+            if (is_first) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) pf[j] = own[j];
+            } else {
+              part(c_first, c, pf);
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(pf[j], v[j]);
+            emit(c, v);
           }
+          if (threadIdx.x == 64) p.counters[c_first] = 0;  // next launch starts from zero
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar);
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (threadIdx.x == 64 && !*abort_ptr) atomicAdd(&p.counters[c_first], 1);
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar);
     }
   }
 
@@ -698,6 +750,7 @@ int launch_nvfp4_gemm(const Nvfp4Launch& L, cudaStream_t stream) {
   p.sk.total = total;
   p.sk.grid = grid;
   p.sk.kb_per_tile = p.kb_per_tile;
+  p.sk.first_poll_ns = debug_force_last_arriver() ? 0 : kFirstPollNs;
   p.sfw = L.b_sf;
   p.sfx = L.a_sf;
   p.alpha = L.alpha;

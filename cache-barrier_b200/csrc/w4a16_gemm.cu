@@ -467,7 +467,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int seg = 0; g < g1; ++tile, kb0 = 0, ++seg) {
       const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
       const int kb1 = kb0 + static_cast<int>(seg_len);
-      const bool first_seg = (g == g0);
       g += seg_len;
       int h, nt, mt;
       decode_tile(p, tile, h, nt, mt);
@@ -476,22 +475,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool whole = (kb0 == 0 && kb1 == KB);
       const int c_first = whole ? 0 : p.sk.owner(tile * KB);
       const int c_last = whole ? 0 : p.sk.owner((tile + 1) * KB - 1);
-      const bool collect = !whole && static_cast<int>(blockIdx.x) == c_first;
+      const int n_contrib = c_last - c_first + 1;
+      const bool is_first = static_cast<int>(blockIdx.x) == c_first;
       constexpr bool kPrefetch = TN <= 32;
       float other[kPrefetch ? TN : 1];
-      bool others_ready = true;
-      if (collect) {
-        // The other contributors handled this tile at the start of their ranges;
-        // wait (bounded) for all of them and pull their parts in before this
-        // CTA's own last MMAs complete.
+      bool last = false;
+      if (!whole) {
+        // Cut tile: the first contributor (whose range ends in this tile; the
+        // others covered it at the start of theirs) polls for the others' parts
+        // for at most kFirstPollNs and then reduces without publishing, pulling
+        // the parts in while its own last MMAs run. If they are not all in by
+        // then, every contributor publishes and the last one to arrive sums the
+        // parts: first contributor's part + the left fold of the others in CTA
+        // order, the same order either way, so results do not depend on timing.
         if (threadIdx.x == kEpiThread0)
-          sh_is_last = wait_counter(&p.counters[c_first], c_last - c_first, abort_ptr, p.status);
+          sh_is_last = poll_counter(&p.counters[c_first], n_contrib - 1, abort_ptr, is_first ? p.sk.first_poll_ns : 0) ? 1 : 0;
         named_bar_sync(1, 128);
-        others_ready = sh_is_last != 0;
+        last = sh_is_last != 0;
         if constexpr (kPrefetch) {
-#pragma unroll
-          for (int j = 0; j < TN; ++j) other[j] = 0.0f;
-          if (others_ready) {
+          if (last && is_first) {
 #pragma unroll
             for (int c = 0; c < TN / 16; ++c) {
               float v[16];
@@ -501,11 +503,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) other[c * 16 + j] = v[j];
             }
-          }
-          // Complete the partial sums now, while this CTA's last MMAs run; the
-          // compiler would otherwise sink the loads to their use after the wait.
+            // Complete the partial sums now, while this CTA's last MMAs run; the
+            // compiler would otherwise sink the loads to their use after the wait.
 #pragma unroll
-          for (int j = 0; j < TN; ++j) asm volatile("" ::"f"(other[j]));
+            for (int j = 0; j < TN; ++j) asm volatile("" ::"f"(other[j]));
+          }
         }
       }
       const bool got = mbar_wait(&tfull_bar[acc], static_cast<uint32_t>((seg >> 1) & 1), abort_ptr, p.status);
@@ -527,44 +529,52 @@ __global__ void __launch_bounds__(kThreads, 1)
             emit_chunk(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - kEpiWarp0) * 512);
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-      } else if (!collect) {
-        // Partial tile, not its first contributor: publish this CTA's part.
-        const int slot = blockIdx.x * 2 + (first_seg ? 0 : 1);
-        float* dst = p.partials + static_cast<long long>(slot) * TN * kBlockN;
-        if (live) {
-#pragma unroll 1
-          for (int c = 0; c < TN / 16; ++c) {
-            uint32_t r[16];
-            __syncwarp();
-            tmem_ld16(d_addr + c * 16, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) dst[(c * 16 + jj) * kBlockN + row] = __uint_as_float(r[jj]);
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (threadIdx.x == kEpiThread0 && !*abort_ptr) atomicAdd(&p.counters[c_first], 1);
       } else {
-        // Partial tile, first contributor: own accumulator + the others' parts.
-        if (live && others_ready) {
-          if constexpr (kPrefetch) {
-#pragma unroll
+        const bool prefetched = kPrefetch && last && is_first;
+        if (!last) {
+          // Publish this CTA's part and count it.
+          const int slot = static_cast<int>(blockIdx.x) * 2 + p.sk.kind(blockIdx.x, tile);
+          float* dst = p.partials + static_cast<long long>(slot) * TN * kBlockN;
+          if (live) {
+#pragma unroll 1
             for (int c = 0; c < TN / 16; ++c) {
               uint32_t r[16];
               __syncwarp();
               tmem_ld16(d_addr + c * 16, r);
               tmem_ld_wait();
-              float v[16];
 #pragma unroll
-              for (int jj = 0; jj < 16; ++jj) v[jj] = __fadd_rn(__uint_as_float(r[jj]), other[c * 16 + jj]);
-              emit_chunk(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - kEpiWarp0) * 512);
+              for (int jj = 0; jj < 16; ++jj) dst[(c * 16 + jj) * kBlockN + row] = __uint_as_float(r[jj]);
+            }
+          }
+          __threadfence();
+          named_bar_sync(1, 128);
+          if (threadIdx.x == kEpiThread0)
+            sh_is_last = (!*abort_ptr && atomicAdd(&p.counters[c_first], 1) == n_contrib - 1) ? 1 : 0;
+          named_bar_sync(1, 128);
+          last = sh_is_last != 0;
+          if (last) __threadfence();
+        }
+        if (last && live) {
+          // part of contributor cc, chunk c of this thread's row
+          auto part = [&](int cc, int c, float (&v)[16]) {
+            const int slot = cc * 2 + p.sk.kind(cc, tile);
+            const float* src = p.partials + static_cast<long long>(slot) * TN * kBlockN + (c * 16) * kBlockN + row;
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) v[jj] = __ldcg(src + jj * kBlockN);
+          };
+          if (prefetched) {
+            if constexpr (kPrefetch) {
+#pragma unroll
+              for (int c = 0; c < TN / 16; ++c) {
+                uint32_t r[16];
+                __syncwarp();
+                tmem_ld16(d_addr + c * 16, r);
+                tmem_ld_wait();
+                float v[16];
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) v[jj] = __fadd_rn(__uint_as_float(r[jj]), other[c * 16 + jj]);
+                emit_chunk(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - kEpiWarp0) * 512);
+              }
             }
           } else {
 #pragma unroll 1
@@ -573,19 +583,40 @@ __global__ void __launch_bounds__(kThreads, 1)
               __syncwarp();
               tmem_ld16(d_addr + c * 16, r);
               tmem_ld_wait();
-              float v[16];
+              float own[16], v[16];
 #pragma unroll
-              for (int jj = 0; jj < 16; ++jj) v[jj] = __uint_as_float(r[jj]);
-              sum_published<TN>(p, c_first + 1, c_last, c, row, v);
+              for (int jj = 0; jj < 16; ++jj) own[jj] = __uint_as_float(r[jj]);
+              // left fold of the parts of c_first + 1 .. c_last
+              for (int cc = c_first + 1; cc <= c_last; ++cc) {
+                float w[16];
+                if (cc == static_cast<int>(blockIdx.x)) {
+#pragma unroll
+                  for (int jj = 0; jj < 16; ++jj) w[jj] = own[jj];
+                } else {
+                  part(cc, c, w);
+                }
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) v[jj] = cc == c_first + 1 ? w[jj] : __fadd_rn(v[jj], w[jj]);
+              }
+              // + the first contributor's part
+              float pf[16];
+              if (is_first) {
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) pf[jj] = own[jj];
+              } else {
+                part(c_first, c, pf);
+              }
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) v[jj] = __fadd_rn(pf[jj], v[jj]);
               emit_chunk(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - kEpiWarp0) * 512);
             }
           }
           if (threadIdx.x == kEpiThread0) p.counters[c_first] = 0;  // next launch starts from zero
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
     }
   }
 
@@ -694,6 +725,7 @@ int launch_w4a16(const W4A16Launch& L, cudaStream_t stream) {
   p.sk.total = total;
   p.sk.grid = grid;
   p.sk.kb_per_tile = p.kb_per_tile;
+  p.sk.first_poll_ns = debug_force_last_arriver() ? 0 : kFirstPollNs;
   p.w = L.w;
   p.scales = L.scales;
   p.scale_dtype = L.scale_dtype;

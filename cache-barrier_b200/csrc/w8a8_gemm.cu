@@ -49,9 +49,6 @@ constexpr int kMinKbPerCta = 8;
 // into shared memory (cp.async) kScaleRing - 1 segments ahead, so a short
 // segment (one k-block) does not wait a memory round trip for its scales.
 constexpr int kScaleRing = 4;
-// How long the first contributor of a cut tile polls for the other
-// contributors' parts before publishing its own instead (last-arriver fallback).
-constexpr unsigned long long kFirstPollNs = 10000;
 
 __device__ __forceinline__ void cp_async_f32(float* dst, const float* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -535,7 +532,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // and bumps the tile's counter; the one that arrives last sums the parts
       // in a fixed order (the first contributor's part + the left fold of the
       // others in CTA order, so fp32 results do not depend on who is last) and
-      // stores the tile. Nobody waits for another CTA. A contributor that already
+      // stores the tile. No CTA waits on another beyond a short bounded poll
+      // whose expiry only changes who reduces. A contributor that already
       // sees every other part published is last without publishing its own; the
       // first contributor then pulls the others' parts in while its last MMAs run.
       const int n_contrib = c_last - c_first + 1;
@@ -549,18 +547,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // then reduces without publishing. If they are not (some CTAs were not
         // resident), it publishes its part and the last arriver finishes the
         // tile: slower, never stuck. The others only look once.
-        if (threadIdx.x == 64) {
-          const int* ctr = &p.counters[c_first];
-          bool done = ld_acquire_gpu(ctr) == n_contrib - 1;
-          if (is_first && !done) {
-            const unsigned long long t0 = global_timer_ns();
-            while (!done && !*abort_ptr && global_timer_ns() - t0 < kFirstPollNs) {
-              __nanosleep(64);
-              done = ld_acquire_gpu(ctr) == n_contrib - 1;
-            }
-          }
-          sh_is_last = done ? 1 : 0;
-        }
+        if (threadIdx.x == 64)
+          sh_is_last = poll_counter(&p.counters[c_first], n_contrib - 1, abort_ptr, is_first ? p.sk.first_poll_ns : 0) ? 1 : 0;
         named_bar_sync(1, 128);
         last = sh_is_last != 0;
         if constexpr (kPrefetch) {
@@ -836,6 +824,7 @@ int launch_w8a8(const W8A8Launch& L, cudaStream_t stream) {
   p.sk.total = total;
   p.sk.grid = grid;
   p.sk.kb_per_tile = p.kb_per_tile;
+  p.sk.first_poll_ns = debug_force_last_arriver() ? 0 : kFirstPollNs;
   p.a_scale = L.a_scale;
   p.as_sb = L.as_sb;
   p.as_sm = L.scale_per_tensor_a ? 0 : 1;

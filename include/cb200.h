@@ -110,6 +110,17 @@ CB_API int cb_workspace_status(void* workspace, int* device_status, cb_stream_t 
    for tests only. */
 CB_API void cb_debug_force_wait_timeout(uint64_t limit_ns);
 
+/* Split-K test hook (no counterpart in the reference). A tile whose k-blocks
+   are split over several CTAs is normally reduced by its first contributor,
+   which polls (for at most 10 us) until the others have published their
+   parts; when they have not (CTAs that were not resident together), every
+   contributor publishes and the last one to arrive reduces the tile. With
+   on != 0 the poll is skipped, so every later W8A8 / FP8 / W4A4 / W4A16 /
+   NVFP4 GEMM launch takes the last-arriver path for every cut tile; both
+   paths sum the parts in the same order, so outputs are bit-identical.
+   Process-wide; for tests only. */
+CB_API void cb_debug_force_last_arriver(int on);
+
 /* ---- activation quantization ------------------------------------------- */
 /* Per-(batch, row) symmetric int8: scale = max(amax/127, 1e-8),
    q = trunc(a/scale + 0.5*sign(a)) (round half away from zero), IEEE-rounded
