@@ -74,6 +74,13 @@ SIGNATURES = {
                            _vp]),
     "cb_w8a8_gemm_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "cb_w8a8_noalloc_status": (_int, [ctypes.POINTER(_int), _vp]),
+    "cb_exec_create": (_int, [_int, ctypes.POINTER(_vp)]),
+    "cb_exec_destroy": (None, [_vp]),
+    "cb_exec_after": (_int, [_vp, _vp]),
+    "cb_exec_before": (_int, [_vp, _vp]),
+    "cb_exec_synchronize": (_int, [_vp, ctypes.POINTER(_int)]),
+    "cb_exec_w8a8_dynamic_host": (_int, [_vp, _vp, _int, _vp, _vp, _i64, _i64, _i64, _vp, _int, _i64, _i64, _i64,
+                                         _i64]),
     "cb_debug_force_wait_timeout": (None, [ctypes.c_uint64]),
     "cb_debug_force_last_arriver": (None, [ctypes.c_int]),
     "cb_w8a8_gemm_dynamic": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _vp, _vp,

@@ -528,3 +528,84 @@ def nvfp4_gemm(a: torch.Tensor, a_sf: torch.Tensor, b: torch.Tensor, b_sf: torch
 def device_status(device: torch.device | None = None) -> int:
     """Synchronising check of the kernels' device-side status words (0 = no timeout)."""
     return POOL.check_status(device)
+
+
+# ---------------------------------------------------------------------------
+# Host-buffer executor (cb_exec_*)
+# ---------------------------------------------------------------------------
+class HostExecutor:
+    """W8A8 dynamic-quant GEMM on host (pinned) activations and outputs.
+
+    Each call enqueues the copy in, the PDL-chained quantizer + GEMM and the
+    copy out on the executor's own streams and returns; consecutive calls
+    overlap one call's copies with the neighbouring calls' kernels. Outputs are
+    valid after ``synchronize()`` (or after work ordered by ``before(stream)``).
+    """
+
+    def __init__(self, device: torch.device | int | None = None):
+        if device is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        elif isinstance(device, int):
+            dev = torch.device("cuda", device)
+        else:
+            dev = device
+        self.device = dev
+        self._lib = L.load()
+        h = ctypes.c_void_p()
+        L.check("cb_exec_create", self._lib.cb_exec_create(dev.index, ctypes.byref(h)))
+        self._h = h
+        self._call = self._lib.cb_exec_w8a8_dynamic_host
+
+    def close(self):
+        if self._h is not None and self._h.value:
+            self._lib.cb_exec_destroy(self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001  (interpreter shutdown)
+            pass
+
+    def after(self, stream: torch.cuda.Stream | None = None):
+        """Later executor work waits for the work already on ``stream``."""
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        L.check("cb_exec_after", self._lib.cb_exec_after(self._h, s.cuda_stream))
+
+    def before(self, stream: torch.cuda.Stream | None = None):
+        """Later work on ``stream`` waits for all executor work enqueued so far."""
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        L.check("cb_exec_before", self._lib.cb_exec_before(self._h, s.cuda_stream))
+
+    def synchronize(self) -> int:
+        """Waits for all executor work; returns the device status word (0 = no timeout)."""
+        st = ctypes.c_int(0)
+        code = self._lib.cb_exec_synchronize(self._h, ctypes.byref(st))
+        if code not in (L.CB_OK, L.CB_ERR_DEVICE_TIMEOUT):
+            L.check("cb_exec_synchronize", code)
+        return st.value
+
+    def w8a8_dynamic_host(self, a_host: torch.Tensor, w_nk: torch.Tensor, w_scale: torch.Tensor,
+                          out_host: torch.Tensor) -> torch.Tensor:
+        """``out_host = w8a8_bmm_full(a_host, w)`` with ``a_host`` f16/bf16 [M, K] / [B, M, K] and
+        ``out_host`` f16/bf16/f32 [M, N] / [B, M, N] contiguous host tensors (pinned for overlap);
+        ``w_nk`` int8 [N, K] / [B, N, K] (K contiguous) and ``w_scale`` fp32 [N] / [B, N] on this device."""
+        if a_host.is_cuda or out_host.is_cuda or not a_host.is_contiguous() or not out_host.is_contiguous():
+            raise ValueError("a_host and out_host must be contiguous host tensors")
+        if not w_nk.is_cuda or w_nk.dtype != torch.int8 or w_nk.stride(-1) != 1 or not w_scale.is_cuda:
+            raise ValueError("w_nk must be an int8 CUDA tensor contiguous along K, w_scale a CUDA tensor")
+        if w_scale.dtype != torch.float32:
+            raise ValueError("w_scale must be fp32")
+        K = a_host.shape[-1]
+        M = a_host.shape[-2]
+        B = a_host.shape[0] if a_host.dim() == 3 else 1
+        N = w_nk.shape[-2]
+        if w_nk.shape[-1] != K or out_host.shape[-1] != N or out_host.numel() != B * M * N:
+            raise ValueError("shape mismatch between a_host, w_nk and out_host")
+        wsb = w_nk.stride(0) if w_nk.dim() == 3 else 0
+        ssb = w_scale.stride(0) if w_scale.dim() == 2 else 0
+        code = self._call(self._h, a_host.data_ptr(), _DTYPE_CODE[a_host.dtype], w_nk.data_ptr(), w_scale.data_ptr(),
+                          wsb, w_nk.stride(-2), ssb, out_host.data_ptr(), _DTYPE_CODE[out_host.dtype], B, M, N, K)
+        if code:
+            L.check("cb_exec_w8a8_dynamic_host", code)
+        return out_host

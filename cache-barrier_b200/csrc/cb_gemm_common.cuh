@@ -29,8 +29,8 @@ struct StreamK {
   long long total;  // tiles * kb_per_tile
   int grid;         // number of CTAs
   int kb_per_tile;
-  // first contributor's poll limit: kFirstPollNs, or 0 under the test hook
-  // that forces the last-arriver path (cb_debug_force_last_arriver)
+  // first contributor's poll limit: kFirstPollNs, or 0 (no poll at all) under
+  // the test hook that forces the last-arriver path (cb_debug_force_last_arriver)
   unsigned long long first_poll_ns;
 
   __host__ __device__ long long start(int c) const { return static_cast<long long>(c) * total / grid; }

@@ -225,6 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t sf_full[kMaxStages];  // the stage's scales are in tensor memory
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
+  __shared__ long long sh_pend_tile;
   __shared__ int sh_issued, sh_consumed, sh_is_last;
   volatile int* abort_ptr = &abort_flag;
 
@@ -474,6 +475,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     long long g = g0;
     long long tile = g0 / KB;
     int kb0 = static_cast<int>(g0 - tile * KB);
+    int pend_old = -1;         // thread 64: counter value its deferred bump returned
+    long long pend_tile = -1;  // thread 64: tile of that bump (-1: none)
     for (; g < g1; ++tile, kb0 = 0) {
       const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
       const int kb1 = kb0 + static_cast<int>(seg_len);
@@ -488,20 +491,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = nt * kBlockN + row;
       const int m0 = mt * TN;
       // Cut tile: the first contributor polls for the others' parts for at most
-      // kFirstPollNs and then reduces without publishing, pulling the parts in
-      // while its own last MMAs run; otherwise every contributor publishes and
-      // the last to arrive reduces. Either way the sum is the first
-      // contributor's part + the left fold of the others in CTA order.
+      // p.sk.first_poll_ns and then reduces without publishing, pulling the
+      // parts in while its own last MMAs run. The others publish and bump the
+      // tile's counter without waiting for the result, which they check once
+      // their other segments are done: the last to arrive (when the first
+      // contributor's poll expired and it published too) reduces then. Either
+      // way the sum is the first contributor's part + the left fold of the
+      // others in CTA order.
       constexpr bool kPrefetch = TN <= 32;
       float other[kPrefetch ? TN : 1];
       bool last = false;
-      if (!whole) {
+      if (!whole && is_first) {
         if (threadIdx.x == 64)
-          sh_is_last = poll_counter(&p.counters[c_first], n_contrib - 1, abort_ptr, is_first ? p.sk.first_poll_ns : 0) ? 1 : 0;
+          sh_is_last =
+              (p.sk.first_poll_ns && poll_counter(&p.counters[c_first], n_contrib - 1, abort_ptr, p.sk.first_poll_ns))
+                  ? 1
+                  : 0;
         named_bar_sync(1, 128);
         last = sh_is_last != 0;
         if constexpr (kPrefetch) {
-          if (last && is_first) {
+          if (last) {
 #pragma unroll
             for (int c = 0; c < TN / 16; ++c) {
               float t[16];
@@ -547,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        const bool prefetched = kPrefetch && last && is_first;
+        const bool prefetched = kPrefetch && last;
         if (!last) {
           // Publish this CTA's part and count it.
           const int slot = static_cast<int>(blockIdx.x) * 2 + p.sk.kind(blockIdx.x, tile);
@@ -565,11 +574,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           __threadfence();
           named_bar_sync(1, 128);
-          if (threadIdx.x == 64)
-            sh_is_last = (!*abort_ptr && atomicAdd(&p.counters[c_first], 1) == n_contrib - 1) ? 1 : 0;
-          named_bar_sync(1, 128);
-          last = sh_is_last != 0;
-          if (last) __threadfence();
+          if (is_first) {
+            // the poll expired: last-arriver fallback, checked at once
+            if (threadIdx.x == 64)
+              sh_is_last = (!*abort_ptr && atomicAdd(&p.counters[c_first], 1) == n_contrib - 1) ? 1 : 0;
+            named_bar_sync(1, 128);
+            last = sh_is_last != 0;
+            if (last) __threadfence();
+          } else if (threadIdx.x == 64 && !*abort_ptr) {
+            // only a CTA's first segment can start inside a tile: one per CTA
+            pend_old = atomicAdd(&p.counters[c_first], 1);
+            pend_tile = tile;
+          }
         }
         if (last && live) {
           // part of contributor cc, chunk c of this thread's row
@@ -623,6 +639,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar);
+    }
+    // Deferred check of the part this CTA published without waiting: if its
+    // bump was the tile's last arrival, the tile is reduced here from the
+    // partial slots (this CTA's part included).
+    if (threadIdx.x == 64) {
+      const int cf = pend_tile >= 0 ? p.sk.owner(pend_tile * KB) : 0;
+      const int cl = pend_tile >= 0 ? p.sk.owner((pend_tile + 1) * KB - 1) : 0;
+      sh_is_last = (pend_tile >= 0 && !*abort_ptr && pend_old == cl - cf) ? 1 : 0;
+      sh_pend_tile = pend_tile;
+    }
+    named_bar_sync(1, 128);
+    if (sh_is_last) {
+      __threadfence();
+      const long long t = sh_pend_tile;
+      const int cf = p.sk.owner(t * KB);
+      const int cl = p.sk.owner((t + 1) * KB - 1);
+      int nt, mt;
+      decode_tile(p, t, nt, mt);
+      const int n = nt * kBlockN + row;
+      const int m0 = mt * TN;
+      auto part = [&](int cc, int c, float (&v)[16]) {
+        const int slot = cc * 2 + p.sk.kind(cc, t);
+        const float* src = p.partials + static_cast<long long>(slot) * TN * kBlockN + (c * 16) * kBlockN + row;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __ldcg(src + j * kBlockN);
+      };
+#pragma unroll 1
+      for (int c = 0; c < TN / 16; ++c) {
+        float v[16], w[16];
+        for (int cc = cf + 1; cc <= cl; ++cc) {
+          part(cc, c, w);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = cc == cf + 1 ? w[j] : __fadd_rn(v[j], w[j]);
+        }
+        part(cf, c, w);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(w[j], v[j]);
+        if (p.vec_out) {
+          uint16_t* stg = epi_stage + (warp - 2) * 512;
+          if (p.out_dtype == CB_DTYPE_BF16)
+            emit_chunk_vec<1>(p, n - lane, lane, m0, c * 16, v, alpha, stg);
+          else
+            emit_chunk_vec<0>(p, n - lane, lane, m0, c * 16, v, alpha, stg);
+        } else {
+          emit_row(p, n, m0, c * 16, v, alpha);
+        }
+      }
+      if (threadIdx.x == 64) p.counters[cf] = 0;  // next launch starts from zero
     }
   }
 

@@ -180,6 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], drain_bar;  // accumulators double-buffered
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
+  __shared__ long long sh_pend_tile;
   __shared__ int sh_issued, sh_consumed, sh_is_last;
   volatile int* abort_ptr = &abort_flag;
 
@@ -464,6 +465,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     long long g = g0;
     long long tile = g0 / KB;
     int kb0 = static_cast<int>(g0 - tile * KB);
+    int pend_old = -1;         // kEpiThread0: counter value its deferred bump returned
+    long long pend_tile = -1;  // kEpiThread0: tile of that bump (-1: none)
     for (int seg = 0; g < g1; ++tile, kb0 = 0, ++seg) {
       const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
       const int kb1 = kb0 + static_cast<int>(seg_len);
@@ -480,20 +483,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr bool kPrefetch = TN <= 32;
       float other[kPrefetch ? TN : 1];
       bool last = false;
-      if (!whole) {
-        // Cut tile: the first contributor (whose range ends in this tile; the
-        // others covered it at the start of theirs) polls for the others' parts
-        // for at most kFirstPollNs and then reduces without publishing, pulling
-        // the parts in while its own last MMAs run. If they are not all in by
-        // then, every contributor publishes and the last one to arrive sums the
-        // parts: first contributor's part + the left fold of the others in CTA
-        // order, the same order either way, so results do not depend on timing.
+      if (!whole && is_first) {
+        // Cut tile. Its first contributor (whose range ends in this tile; the
+        // others covered it at the start of theirs, so they are done first when
+        // all CTAs run together) polls for the others' parts for at most
+        // p.sk.first_poll_ns and then reduces without publishing its own,
+        // pulling the parts in while its last MMAs run. Every other contributor
+        // publishes its part and bumps the tile's counter without waiting for
+        // the atomic's result; it looks at that result once its other segments
+        // are done and, if it arrived last (the first contributor gave up its
+        // poll and published too), reduces the tile then. Both reductions sum
+        // in one order (the first contributor's part + the left fold of the
+        // others in CTA order), so results do not depend on who reduces.
         if (threadIdx.x == kEpiThread0)
-          sh_is_last = poll_counter(&p.counters[c_first], n_contrib - 1, abort_ptr, is_first ? p.sk.first_poll_ns : 0) ? 1 : 0;
+          sh_is_last =
+              (p.sk.first_poll_ns && poll_counter(&p.counters[c_first], n_contrib - 1, abort_ptr, p.sk.first_poll_ns))
+                  ? 1
+                  : 0;
         named_bar_sync(1, 128);
         last = sh_is_last != 0;
         if constexpr (kPrefetch) {
-          if (last && is_first) {
+          if (last) {
 #pragma unroll
             for (int c = 0; c < TN / 16; ++c) {
               float v[16];
@@ -530,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        const bool prefetched = kPrefetch && last && is_first;
+        const bool prefetched = kPrefetch && last;
         if (!last) {
           // Publish this CTA's part and count it.
           const int slot = static_cast<int>(blockIdx.x) * 2 + p.sk.kind(blockIdx.x, tile);
@@ -548,11 +558,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           __threadfence();
           named_bar_sync(1, 128);
-          if (threadIdx.x == kEpiThread0)
-            sh_is_last = (!*abort_ptr && atomicAdd(&p.counters[c_first], 1) == n_contrib - 1) ? 1 : 0;
-          named_bar_sync(1, 128);
-          last = sh_is_last != 0;
-          if (last) __threadfence();
+          if (is_first) {
+            // the poll expired: last-arriver fallback, checked at once
+            if (threadIdx.x == kEpiThread0)
+              sh_is_last = (!*abort_ptr && atomicAdd(&p.counters[c_first], 1) == n_contrib - 1) ? 1 : 0;
+            named_bar_sync(1, 128);
+            last = sh_is_last != 0;
+            if (last) __threadfence();
+          } else if (threadIdx.x == kEpiThread0 && !*abort_ptr) {
+            // only a CTA's first segment can start inside a tile: one per CTA
+            pend_old = atomicAdd(&p.counters[c_first], 1);
+            pend_tile = tile;
+          }
         }
         if (last && live) {
           // part of contributor cc, chunk c of this thread's row
@@ -617,6 +634,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+    // Deferred check of the part this CTA published without waiting: if its
+    // bump was the tile's last arrival, the tile is reduced here from the
+    // partial slots (this CTA's part included).
+    if (threadIdx.x == kEpiThread0) {
+      const int cf = pend_tile >= 0 ? p.sk.owner(pend_tile * KB) : 0;
+      const int cl = pend_tile >= 0 ? p.sk.owner((pend_tile + 1) * KB - 1) : 0;
+      sh_is_last = (pend_tile >= 0 && !*abort_ptr && pend_old == cl - cf) ? 1 : 0;
+      sh_pend_tile = pend_tile;
+    }
+    named_bar_sync(1, 128);
+    if (sh_is_last) {
+      __threadfence();
+      const long long t = sh_pend_tile;
+      const int cf = p.sk.owner(t * KB);
+      const int cl = p.sk.owner((t + 1) * KB - 1);
+      int h, nt, mt;
+      decode_tile(p, t, h, nt, mt);
+      auto part = [&](int cc, int c, float (&v)[16]) {
+        const int slot = cc * 2 + p.sk.kind(cc, t);
+        const float* src = p.partials + static_cast<long long>(slot) * TN * kBlockN + (c * 16) * kBlockN + row;
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) v[jj] = __ldcg(src + jj * kBlockN);
+      };
+#pragma unroll 1
+      for (int c = 0; c < TN / 16; ++c) {
+        float v[16], w[16];
+        for (int cc = cf + 1; cc <= cl; ++cc) {
+          part(cc, c, w);
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) v[jj] = cc == cf + 1 ? w[jj] : __fadd_rn(v[jj], w[jj]);
+        }
+        part(cf, c, w);
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) v[jj] = __fadd_rn(w[jj], v[jj]);
+        emit_chunk(p, h, nt * kBlockN + row, lane, mt * TN, c * 16, v, epi_stage + (warp - kEpiWarp0) * 512);
+      }
+      if (threadIdx.x == kEpiThread0) p.counters[cf] = 0;  // next launch starts from zero
     }
   }
 

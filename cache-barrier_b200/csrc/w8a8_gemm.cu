@@ -263,6 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
+  __shared__ long long sh_pend_tile;
   __shared__ int sh_issued, sh_consumed, sh_is_last;
   // scales of the next kScaleRing segments (epilogue, token tiles up to 32)
   __shared__ float ws_ring[kScaleRing][kBlockN];
@@ -298,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     abort_flag = 0;
     sh_issued = 0;
     sh_consumed = 0;
-    sh_is_last = 0;  // cut tiles: whether this CTA is the last contributor
+    sh_is_last = 0;  // cut tiles: whether this CTA reduces the tile
     fence_mbar_init();
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_a);
@@ -476,6 +477,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     long long g = g0;
     long long tile = g0 / KB;
     int kb0 = static_cast<int>(g0 - tile * KB);
+    int pend_old = -1;         // thread 64: counter value its deferred bump returned
+    long long pend_tile = -1;  // thread 64: tile of that bump (-1: none)
     constexpr bool kPrefetch = TN <= 32;
     const long long last_tile = (g1 - 1) / KB;
     // Copies (cp.async, one commit group per segment) of segment t's scales into
@@ -528,31 +531,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (p.bias && n < p.N) bias_pre = load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n);
       }
-      // Cut tile: last-arriver reduction. Every contributor publishes its part
-      // and bumps the tile's counter; the one that arrives last sums the parts
-      // in a fixed order (the first contributor's part + the left fold of the
-      // others in CTA order, so fp32 results do not depend on who is last) and
-      // stores the tile. No CTA waits on another beyond a short bounded poll
-      // whose expiry only changes who reduces. A contributor that already
-      // sees every other part published is last without publishing its own; the
-      // first contributor then pulls the others' parts in while its last MMAs run.
+      // Cut tile. Its first contributor (whose range ends in this tile; the
+      // others covered it at the start of theirs, so they are done first when
+      // all CTAs run together) polls for the others' parts for at most
+      // p.sk.first_poll_ns and then reduces without publishing its own, pulling
+      // the parts in while its last MMAs run. Every other contributor publishes
+      // its part and bumps the tile's counter without waiting for the atomic's
+      // result; it looks at that result once its other segments are done, and
+      // if it arrived last (the first contributor gave up its poll and
+      // published too) it reduces the tile then. Both reductions sum in one
+      // order (the first contributor's part + the left fold of the others in
+      // CTA order), so results do not depend on who reduces, and no CTA waits
+      // on another beyond the bounded poll.
       const int n_contrib = c_last - c_first + 1;
       const bool is_first = static_cast<int>(blockIdx.x) == c_first;
       bool last = false;
       Acc other[kPrefetch ? TN : 1];
-      if (!whole) {
-        // The first contributor (whose range ends in this tile; the others
-        // covered it at the start of theirs) polls for their parts for at most
-        // kFirstPollNs: co-resident contributors are done by then, and this CTA
-        // then reduces without publishing. If they are not (some CTAs were not
-        // resident), it publishes its part and the last arriver finishes the
-        // tile: slower, never stuck. The others only look once.
+      if (!whole && is_first) {
         if (threadIdx.x == 64)
-          sh_is_last = poll_counter(&p.counters[c_first], n_contrib - 1, abort_ptr, is_first ? p.sk.first_poll_ns : 0) ? 1 : 0;
+          sh_is_last =
+              (p.sk.first_poll_ns && poll_counter(&p.counters[c_first], n_contrib - 1, abort_ptr, p.sk.first_poll_ns))
+                  ? 1
+                  : 0;
         named_bar_sync(1, 128);
         last = sh_is_last != 0;
         if constexpr (kPrefetch) {
-          if (last && is_first) {
+          if (last) {
 #pragma unroll
             for (int c = 0; c < TN / 16; ++c) {
               Acc v[16];
@@ -637,11 +641,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           __threadfence();
           named_bar_sync(1, 128);
-          if (threadIdx.x == 64)
-            sh_is_last = (!*abort_ptr && atomicAdd(&p.counters[c_first], 1) == n_contrib - 1) ? 1 : 0;
-          named_bar_sync(1, 128);
-          last = sh_is_last != 0;
-          if (last) __threadfence();
+          if (is_first) {
+            // the poll expired: last-arriver fallback, checked at once
+            if (threadIdx.x == 64)
+              sh_is_last = (!*abort_ptr && atomicAdd(&p.counters[c_first], 1) == n_contrib - 1) ? 1 : 0;
+            named_bar_sync(1, 128);
+            last = sh_is_last != 0;
+            if (last) __threadfence();
+          } else if (threadIdx.x == 64 && !*abort_ptr) {
+            // only a CTA's first segment can start inside a tile, so there is
+            // at most one of these per CTA
+            pend_old = atomicAdd(&p.counters[c_first], 1);
+            pend_tile = tile;
+          }
         }
         if (last && live) {
           // part of contributor cc, chunk c of this thread's row
@@ -713,6 +725,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       }
+    }
+    // Deferred check of the part this CTA published without waiting: if its
+    // bump was the tile's last arrival, the tile is reduced here, every part
+    // (this CTA's included) read back from the partial slots.
+    if (threadIdx.x == 64) {
+      const int cf = pend_tile >= 0 ? p.sk.owner(pend_tile * KB) : 0;
+      const int cl = pend_tile >= 0 ? p.sk.owner((pend_tile + 1) * KB - 1) : 0;
+      sh_is_last = (pend_tile >= 0 && !*abort_ptr && pend_old == cl - cf) ? 1 : 0;
+      sh_pend_tile = pend_tile;
+    }
+    named_bar_sync(1, 128);
+    if (sh_is_last) {
+      __threadfence();
+      const long long t = sh_pend_tile;
+      const int cf = p.sk.owner(t * KB);
+      const int cl = p.sk.owner((t + 1) * KB - 1);
+      int h, nt, mt;
+      decode_tile(p, t, h, nt, mt);
+      auto part = [&](int cc, int c, Acc (&v)[16]) {
+        const int slot = cc * 2 + p.sk.kind(cc, t);
+        const Acc* src =
+            static_cast<const Acc*>(p.partials) + static_cast<long long>(slot) * TN * kBlockN + (c * 16) * kBlockN + row;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __ldcg(src + j * kBlockN);
+      };
+#pragma unroll 1
+      for (int c = 0; c < TN / 16; ++c) {
+        Acc v[16], w[16];
+        for (int cc = cf + 1; cc <= cl; ++cc) {
+          part(cc, c, w);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = cc == cf + 1 ? w[j] : v[j] + w[j];
+        }
+        part(cf, c, w);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = w[j] + v[j];
+        emit_row_any<TN, Acc>(p, h, nt * kBlockN + row, lane, mt * TN, c * 16, v, epi_stage + (warp - 2) * 512);
+      }
+      if (threadIdx.x == 64) p.counters[cf] = 0;  // next launch starts from zero
     }
   }
 

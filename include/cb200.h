@@ -200,6 +200,42 @@ CB_API int cb_w8a8_gemm_noalloc(const int8_t* aq, const float* a_scale, const in
    cb_workspace_status for callers that hold no workspace. */
 CB_API int cb_w8a8_noalloc_status(int* device_status, cb_stream_t stream);
 
+/* ---- host-buffer executor (no counterpart in the reference) -------------
+   For callers whose activations and results live in host memory (a serving
+   loop, a foreign-language binding): one call copies the activations in,
+   runs cb_w8a8_gemm_dynamic and copies the result back, all enqueued on the
+   executor's own three streams (copy-in, compute, copy-out) with a ring of two
+   device buffer sets, so consecutive calls overlap one call's copies with the
+   neighbouring calls' kernels. Calls return once the work is enqueued; host
+   buffers must stay valid (and the output unread) until cb_exec_synchronize
+   or until work ordered after the call by cb_exec_before has completed. Use
+   page-locked (pinned) host memory: with pageable memory the copies still
+   give the right result but block the calling thread. An executor owns its
+   device buffers (grown on demand, which first waits for its work in flight)
+   and is not thread-safe: one thread at a time per executor. */
+typedef struct cb_exec cb_exec;
+CB_API int cb_exec_create(int device, cb_exec** exec);
+CB_API void cb_exec_destroy(cb_exec* exec);
+/* Work enqueued on the executor after this call waits for the work enqueued on
+   `stream` before it. */
+CB_API int cb_exec_after(cb_exec* exec, cb_stream_t stream);
+/* Work enqueued on `stream` after this call waits for all work the executor
+   has enqueued so far (copies back to the host included). */
+CB_API int cb_exec_before(cb_exec* exec, cb_stream_t stream);
+/* Waits for all of the executor's work; then reads and clears its workspace
+   status word like cb_workspace_status (CB_ERR_DEVICE_TIMEOUT if a kernel
+   recorded an expired wait). */
+CB_API int cb_exec_synchronize(cb_exec* exec, int* device_status);
+/* out_host[b, m, n] = w8a8_bmm_full(a_host, w)[b, m, n]: a_host f16/bf16
+   [batch, M, K] and out_host [batch, M, N] (f16/bf16/f32) contiguous host
+   arrays; w int8 [batch, N, K] (K contiguous) and w_scale fp32 [batch, N] in
+   device memory, with element strides w_stride_b, w_stride_n and
+   w_scale_stride_b. Same arithmetic and results as cb_w8a8_gemm_dynamic. */
+CB_API int cb_exec_w8a8_dynamic_host(cb_exec* exec, const void* a_host, int a_dtype, const int8_t* w,
+                                     const float* w_scale, int64_t w_stride_b, int64_t w_stride_n,
+                                     int64_t w_scale_stride_b, void* out_host, int out_dtype, int64_t batch,
+                                     int64_t M, int64_t N, int64_t K);
+
 /* ---- FP8 (e4m3) W8A8 GEMM ----------------------------------------------- */
 /* The reference measures its W8A8 path against vLLM's fp8 cutlass_scaled_mm
    on e4m3 operands (profiling/dense_qwen/bench_l2_boundary.py:54-57, 66-68;
