@@ -5,9 +5,17 @@
 // (tile-major) and cut into G equal contiguous ranges, one per CTA, so every SM
 // streams the same number of weight bytes whatever the shape. A tile whose
 // k-blocks fall in one CTA's range is finished by that CTA; a tile cut by a
-// range boundary is reduced deterministically: each contributor writes its
-// partial accumulator to its own slot, and the last one to arrive (per-tile
-// arrival counter) sums the slots in CTA order and runs the epilogue.
+// range boundary is reduced deterministically. The tile's first contributor
+// (lowest CTA index; its range ends in the tile) keeps its part in tensor
+// memory; every other contributor writes its part to its own slot and bumps
+// the tile's arrival counter, keeping the value its atomic returned. The first
+// contributor polls that counter for a short bounded time and, when every
+// part is in, sums the slots in CTA order and runs the epilogue. If the poll
+// expires it publishes its part and bumps the counter too, and whichever
+// contributor's bump completes the count (the first at once, or another one
+// when it checks its returned value at the end of its range) reduces the tile
+// from the slots in the same order. No CTA ever waits for one that may not be
+// running, and the bits do not depend on who reduces.
 #pragma once
 
 #include <cstdint>
@@ -44,6 +52,27 @@ struct StreamK {
     return start(c) >= tile * kb_per_tile ? 0 : 1;
   }
 };
+
+// (batch h, n-tile, m-tile) of a tile index (tiles ordered batch-major, m-tile
+// fastest). 32-bit divisions when the index fits: the epilogues decode tiles
+// per segment, and with one k-block per tile (short K) 64-bit divisions would
+// dominate their time.
+__device__ __forceinline__ void split_tile(long long tile, int m_tiles, int n_tiles, int& h, int& nt, int& mt) {
+  if (tile < 0x7fffffffLL) {
+    const unsigned t = static_cast<unsigned>(tile), ml = static_cast<unsigned>(m_tiles);
+    const unsigned nl = static_cast<unsigned>(n_tiles);
+    const unsigned r = t / ml;
+    mt = static_cast<int>(t - r * ml);
+    const unsigned hh = r / nl;
+    nt = static_cast<int>(r - hh * nl);
+    h = static_cast<int>(hh);
+    return;
+  }
+  mt = static_cast<int>(tile % m_tiles);
+  const long long r = tile / m_tiles;
+  nt = static_cast<int>(r % n_tiles);
+  h = static_cast<int>(r / n_tiles);
+}
 
 // Coordinates of a k-block, advanced without division (the producer walks its
 // range one k-block at a time; 64-bit divisions per step would dominate it).

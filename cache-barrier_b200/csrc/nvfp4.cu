@@ -154,8 +154,8 @@ struct Params {
 };
 
 __device__ __forceinline__ void decode_tile(const Params& p, long long tile, int& nt, int& mt) {
-  mt = static_cast<int>(tile % p.m_tiles);
-  nt = static_cast<int>(tile / p.m_tiles);
+  int h;
+  split_tile(tile, p.m_tiles, p.n_tiles, h, nt, mt);  // one batch entry: h = 0
 }
 
 template <int TN>

@@ -81,10 +81,7 @@ struct Params {
 };
 
 __device__ __forceinline__ void decode_tile(const Params& p, long long tile, int& h, int& nt, int& mt) {
-  mt = static_cast<int>(tile % p.m_tiles);
-  long long r = tile / p.m_tiles;
-  nt = static_cast<int>(r % p.n_tiles);
-  h = static_cast<int>(r / p.n_tiles);
+  split_tile(tile, p.m_tiles, p.n_tiles, h, nt, mt);
 }
 
 __device__ __forceinline__ void emit_row(const Params& p, int h, int n, int m0, int t0, const float (&v)[16]) {

@@ -19,8 +19,9 @@
 //              stores (16-bit outputs staged per warp in shared memory and
 //              written as 16-byte vectors), split-K slot writes and the
 //              deterministic reduction.
-//   warp 6     stage waiter: waits for each stage's TMA bytes and hands the
-//              k-block to warp 1 through a named barrier, so the MMA issuer
+//   warp 6     stage waiter: waits for each stage's TMA bytes (and, at a tile's
+//              first k-block, for a free accumulator of the TMEM ring) and hands
+//              the k-block to warp 1 through a named barrier, so the MMA issuer
 //              never waits on shared memory.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -112,10 +113,7 @@ struct Params {
 };
 
 __device__ __forceinline__ void decode_tile(const Params& p, long long tile, int& h, int& nt, int& mt) {
-  mt = static_cast<int>(tile % p.m_tiles);
-  long long r = tile / p.m_tiles;
-  nt = static_cast<int>(r % p.n_tiles);
-  h = static_cast<int>(r / p.n_tiles);
+  split_tile(tile, p.m_tiles, p.n_tiles, h, nt, mt);
 }
 
 template <int TN, typename Acc>
@@ -255,12 +253,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kATileBytes = TN * kBlockK;
   constexpr uint32_t kStageBytes = kWTileBytes + kATileBytes;
   constexpr uint32_t kAccCols = TN < 32 ? 32 : TN;
-  constexpr uint32_t kTmemCols = 2 * kAccCols;  // two accumulators: a tile's MMAs overlap the previous tile's epilogue
+  // Accumulator ring in TMEM: segment s uses accumulator s % kNumAcc, so the
+  // MMAs run up to kNumAcc - 1 segments ahead of the epilogue (short-K problems
+  // have one k-block per tile, and the epilogue's per-tile latency would
+  // otherwise gate every tile's MMAs).
+  constexpr int kNumAcc = static_cast<int>(512 / kAccCols) < 8 ? static_cast<int>(512 / kAccCols) : 8;
+  constexpr uint32_t kTmemCols = kNumAcc * kAccCols;
+  static_assert((kNumAcc & (kNumAcc - 1)) == 0 && kTmemCols <= 512, "accumulator ring must fit TMEM");
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
-  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], drain_bar;
+  __shared__ __align__(8) uint64_t tfull_bar[kNumAcc], tempty_bar[kNumAcc], drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ long long sh_pend_tile;
@@ -291,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kNumAcc; ++a) {
       mbar_init(&tfull_bar[a], 1);
       mbar_init(&tempty_bar[a], 4);
     }
@@ -379,23 +383,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage = 0;
     int consumed = 0;
     int n_tfull = 0;
-    bool bad = false;
     long long g = g0;
     int kb_first = static_cast<int>(g0 % KB);
     for (int seg = 0; g < g1; ++seg) {
       const long long seg_len = (KB - kb_first) < (g1 - g) ? (KB - kb_first) : (g1 - g);
       const long long seg_end = g + seg_len;
       kb_first = 0;
-      // Segment seg accumulates into accumulator seg % 2, free once the epilogue
-      // drained the segment two back.
-      const int acc = seg & 1;
+      // Segment seg accumulates into accumulator seg % kNumAcc; the stage waiter
+      // hands the segment's first k-block over only once the epilogue has
+      // drained that accumulator's previous segment.
+      const int acc = seg & (kNumAcc - 1);
       const uint32_t tmem_acc = tmem_d + acc * kAccCols;
-      if (lane == 0 && !bad)
-        bad = !mbar_wait(&tempty_bar[acc], static_cast<uint32_t>(((seg >> 1) & 1) ^ 1), abort_ptr, p.status);
-      bad = __shfl_sync(0xffffffffu, bad, 0);
       bool stop = false;
       for (bool first = true; g < seg_end; ++g, first = false) {
-        if (named_bar_or(kHandoffBar, 64, bad)) {
+        if (named_bar_or(kHandoffBar, 64, false)) {
           stop = true;
           break;
         }
@@ -431,32 +432,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // Every commit arrival lane 0 issued must land before the CTA exits (an
     // arrive on released shared memory faults): the releases of the last S
-    // stages and the last accumulator hand-off. One lane per barrier, so the
-    // waits overlap instead of adding up.
+    // stages (lanes 0..S-1, S <= 16) and the last kNumAcc accumulator hand-offs
+    // (lanes 16..16+kNumAcc-1). One lane per barrier, so the waits overlap
+    // instead of adding up.
     consumed = __shfl_sync(0xffffffffu, consumed, 0);
     n_tfull = __shfl_sync(0xffffffffu, n_tfull, 0);
     {
       const int j = consumed - 1 - lane;  // lane l waits the (l+1)-th most recent stage release
       if (lane < S && j >= 0) mbar_wait(&empty_bar[j % S], static_cast<uint32_t>((j / S) & 1), nullptr, p.status);
-      const int t = n_tfull - 1 - (lane - 30);  // lanes 30, 31: the last two accumulator hand-offs
-      if (lane >= 30 && t >= 0) mbar_wait(&tfull_bar[t & 1], static_cast<uint32_t>((t >> 1) & 1), nullptr, p.status);
+      const int t = n_tfull - 1 - (lane - 16);  // lanes 16.. : the last kNumAcc accumulator hand-offs
+      if (lane >= 16 && lane < 16 + kNumAcc && t >= 0)
+        mbar_wait(&tfull_bar[t & (kNumAcc - 1)], static_cast<uint32_t>((t / kNumAcc) & 1), nullptr, p.status);
     }
     __syncwarp();
   } else if (warp == kWaiterWarp) {
     // ---------------- stage waiter ----------------
-    // Waits for each stage's TMA bytes and hands the k-block to the MMA warp
-    // (one named-barrier round per k-block, the same count as the MMA warp's).
+    // Waits for each stage's TMA bytes (and, before a segment's first k-block,
+    // for the epilogue to free the segment's accumulator) and hands the k-block
+    // to the MMA warp: one named-barrier round per k-block, the same count as
+    // the MMA warp's.
     int stage = 0;
     uint32_t phase = 0;
+    int kb = static_cast<int>(g0 % KB);  // k-block within its tile
+    int seg = -1;
     for (long long g = g0; g < g1; ++g) {
       bool bad = false;
-      if (lane == 0) bad = !mbar_wait(&full_bar[stage], phase, abort_ptr, p.status);
+      if (g == g0 || kb == 0) ++seg;
+      if (lane == 0) {
+        if (g == g0 || kb == 0)
+          bad = !mbar_wait(&tempty_bar[seg & (kNumAcc - 1)], static_cast<uint32_t>(((seg / kNumAcc) & 1) ^ 1),
+                           abort_ptr, p.status);
+        if (!bad) bad = !mbar_wait(&full_bar[stage], phase, abort_ptr, p.status);
+      }
       bad = __shfl_sync(0xffffffffu, bad, 0);
       if (named_bar_or(kHandoffBar, 64, bad)) break;
       if (++stage == S) {
         stage = 0;
         phase ^= 1u;
       }
+      if (++kb == KB) kb = 0;
     }
     __syncwarp();
   } else {
@@ -572,9 +586,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      const int acc = seg & 1;
+      const int acc = seg & (kNumAcc - 1);
       const uint32_t lane_addr = lane_addr0 + acc * kAccCols;
-      const bool got = mbar_wait(&tfull_bar[acc], static_cast<uint32_t>((seg >> 1) & 1), abort_ptr, p.status);
+      const bool got = mbar_wait(&tfull_bar[acc], static_cast<uint32_t>((seg / kNumAcc) & 1), abort_ptr, p.status);
       ++seg;
       const bool live = __all_sync(0xffffffffu, got);
       tc_fence_after();
