@@ -74,6 +74,35 @@ __device__ __forceinline__ void split_tile(long long tile, int m_tiles, int n_ti
   h = static_cast<int>(r / n_tiles);
 }
 
+// (batch, n-tile, m-tile) of consecutive tiles, advanced without division (an
+// epilogue walks its range one tile per segment).
+struct TileCursor {
+  int h, nt, mt;
+  __device__ __forceinline__ void seek(long long tile, int m_tiles, int n_tiles) {
+    split_tile(tile, m_tiles, n_tiles, h, nt, mt);
+  }
+  __device__ __forceinline__ void next(int m_tiles, int n_tiles) {
+    if (++mt == m_tiles) {
+      mt = 0;
+      if (++nt == n_tiles) {
+        nt = 0;
+        ++h;
+      }
+    }
+  }
+};
+
+// First and last contributor of a cut tile, packed as c_first | c_last << 32.
+// Out of line so that its two 64-bit divisions run only for cut tiles (at most
+// the first and the last segment of a CTA's range), never speculatively.
+static __device__ __noinline__ long long cut_contributors(long long total, int grid, int kb_per_tile, long long tile) {
+  const long long first_kb = tile * kb_per_tile;
+  const long long last_kb = first_kb + kb_per_tile - 1;
+  const long long cf = ((first_kb + 1) * grid - 1) / total;
+  const long long cl = ((last_kb + 1) * grid - 1) / total;
+  return cf | (cl << 32);
+}
+
 // Coordinates of a k-block, advanced without division (the producer walks its
 // range one k-block at a time; 64-bit divisions per step would dominate it).
 struct KCursor {

@@ -10,15 +10,15 @@
 // decode batches of 1..32 tokens still fill 128-row MMAs. Work is split over
 // all SMs with the stream-K partition of cb_gemm_common.cuh.
 //
-// Warp roles (224 threads):
+// Warp roles (352 threads):
 //   warp 0     TMA producer (one lane): weight tile 128 x 128 B + token tile TN x 128 B
 //              per k-block, 128-byte swizzle. Weight loads of the first ring pass
 //              are issued before griddepcontrol.wait; token loads after it.
 //   warp 1     TMEM allocation + MMA issuer (one lane), 4 MMAs (K = 32) per k-block.
-//   warps 2-5  epilogue: tcgen05.ld of the accumulator, scaling, bf16/f16/f32
-//              stores (16-bit outputs staged per warp in shared memory and
-//              written as 16-byte vectors), split-K slot writes and the
-//              deterministic reduction.
+//   warps 2-5, 7-10  two epilogue groups taking alternate tiles: tcgen05.ld of
+//              the accumulator, scaling, bf16/f16/f32 stores (16-bit outputs
+//              staged per warp in shared memory and written as 16-byte
+//              vectors), split-K slot writes and the deterministic reduction.
 //   warp 6     stage waiter: waits for each stage's TMA bytes (and, at a tile's
 //              first k-block, for a free accumulator of the TMEM ring) and hands
 //              the k-block to warp 1 through a named barrier, so the MMA issuer
@@ -38,9 +38,19 @@ namespace {
 
 constexpr int kBlockN = 128;   // weight rows per tile (MMA M)
 constexpr int kBlockK = 128;   // int8 K per k-block (one 128-byte swizzle row)
-constexpr int kThreads = 224;
+// Threads of the kernel with EG epilogue groups: producer, MMA, EG x 4
+// epilogue warps and the stage waiter.
+constexpr int threads_for(int eg) { return eg == 2 ? 352 : 224; }
+// Largest k-blocks per tile for which the two-group epilogue is launched: with
+// short K every tile is a segment of one or a few k-blocks and the epilogue's
+// per-tile latency sets the rate; with long K one group keeps up, and the
+// smaller CTA leaves registers for a kernel overlapping it (the activation
+// quantizer under programmatic dependent launch).
+constexpr int kMaxKbTwoGroups = 8;
 constexpr int kWaiterWarp = 6;
-constexpr int kHandoffBar = 2;  // named barrier: MMA warp + stage waiter (barrier 1 is the epilogue's)
+constexpr int kHandoffBar = 2;  // named barrier: MMA warp + stage waiter
+// Named barriers of the two epilogue warpgroups (128 threads each).
+constexpr int kEpiBar0 = 1, kEpiBar1 = 3;
 constexpr uint32_t kWTileBytes = kBlockN * kBlockK;
 // Fewest k-blocks a CTA takes when the problem has fewer k-blocks than that
 // many per SM: small GEMMs then run on fewer CTAs instead of cutting each tile
@@ -245,8 +255,8 @@ __device__ __forceinline__ void sum_published(const Params& p, int c_lo, int c_h
   }
 }
 
-template <int TN, int KIND>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int TN, int KIND, int EG>
+__global__ void __launch_bounds__(threads_for(EG), 1)
     w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                      const Params p) {
   using Acc = typename AccOf<KIND>::T;
@@ -267,17 +277,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t tfull_bar[kNumAcc], tempty_bar[kNumAcc], drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
-  __shared__ long long sh_pend_tile;
-  __shared__ int sh_issued, sh_consumed, sh_is_last;
+  __shared__ long long sh_pend_tile[2];
+  __shared__ int sh_issued, sh_consumed;
+  __shared__ int sh_is_last[2];  // per epilogue group: whether this CTA reduces the cut tile at hand
   // scales of the next kScaleRing segments (epilogue, token tiles up to 32)
-  __shared__ float ws_ring[kScaleRing][kBlockN];
-  __shared__ float as_ring[kScaleRing][TN <= 32 ? TN : 1];
+  __shared__ __align__(16) float ws_ring[EG][kScaleRing][kBlockN];
+  __shared__ __align__(16) float as_ring[EG][kScaleRing][TN <= 32 ? TN : 4];
   volatile int* abort_ptr = &abort_flag;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_w = smem;
   uint8_t* smem_a = smem + p.stages * kWTileBytes;
-  // per epilogue warp: 16 tokens x 32 columns of 16-bit output (vector-store staging)
+  // per epilogue warp (8): 16 tokens x 32 columns of 16-bit output (vector-store staging)
   uint16_t* epi_stage = reinterpret_cast<uint16_t*>(smem_a + p.stages * (TN * kBlockK));
 
   const int warp = threadIdx.x >> 5;
@@ -303,7 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     abort_flag = 0;
     sh_issued = 0;
     sh_consumed = 0;
-    sh_is_last = 0;  // cut tiles: whether this CTA reduces the tile
+    sh_is_last[0] = 0;
+    sh_is_last[1] = 0;
     fence_mbar_init();
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_a);
@@ -474,10 +486,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    // Control flow is uniform across the 128 epilogue threads even after an
-    // aborted wait: work is skipped, but every named barrier is still reached
-    // by all of them, so no thread can be left waiting on a barrier.
+    // ---------------- epilogue (group 0: warps 2..5, group 1: warps 7..10) ----------------
+    // The two groups take alternate segments (group s % 2 drains segment s),
+    // so one group's scale loads, TMEM reads and stores overlap the other's;
+    // with one k-block per tile (short K) a single group's per-tile latency
+    // would set the kernel's rate. Each accumulator of the ring belongs to one
+    // group (the ring size is even). Control flow is uniform across a group's
+    // 128 threads even after an aborted wait: work is skipped, but every named
+    // barrier is still reached by all of them, so no thread can be left
+    // waiting on a barrier.
+    const int grp = (EG == 2 && warp > kWaiterWarp) ? 1 : 0;
+    const int leader = grp == 0 ? 64 : (kWaiterWarp + 1) * 32;  // runs the group's counter operations
+    const int ebar = grp == 0 ? kEpiBar0 : kEpiBar1;
+    uint16_t* const stg = epi_stage + (grp == 0 ? warp - 2 : warp - 3) * 512;  // this warp's staging
     pdl_wait_primary();
     // Failure-detection test hook (cb_debug_force_wait_timeout): one thread
     // waits, with a short limit, on a workspace word that nothing ever sets, so
@@ -491,37 +512,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     long long g = g0;
     long long tile = g0 / KB;
     int kb0 = static_cast<int>(g0 - tile * KB);
-    int pend_old = -1;         // thread 64: counter value its deferred bump returned
-    long long pend_tile = -1;  // thread 64: tile of that bump (-1: none)
+    int pend_old = -1;         // leader: counter value its deferred bump returned
+    long long pend_tile = -1;  // leader: tile of that bump (-1: none)
     constexpr bool kPrefetch = TN <= 32;
     const long long last_tile = (g1 - 1) / KB;
-    // Copies (cp.async, one commit group per segment) of segment t's scales into
-    // ring slot t % kScaleRing: each thread its row's w_scale, threads 0..TN-1
-    // one a_scale each.
+    // Copies (cp.async, one commit group per own segment) of the scales of the
+    // group's k-th own segment into its ring slot k % kScaleRing: each thread
+    // its row's w_scale, threads 0..TN-1 one a_scale each.
+    // Tile coordinates of the current segment (cur) and of the own segment
+    // whose scales are copied next (pre, kScaleRing - 1 own segments ahead:
+    // each own segment is two tiles on).
+    TileCursor cur, pre;
+    cur.seek(tile, p.m_tiles, p.n_tiles);
+    pre = cur;
+    if (grp) pre.next(p.m_tiles, p.n_tiles);
     auto issue_scales = [&](long long t, int slot) {
       if (t <= last_tile && !p.raw_f32) {
-        int hh, nnt, mmt;
-        decode_tile(p, t, hh, nnt, mmt);
-        const int nn = nnt * kBlockN + row;
-        if (nn < p.N) cp_async_f32(&ws_ring[slot][row], p.w_scale + hh * p.ws_sb + nn * p.ws_sn);
-        const int mm = mmt * TN + row;
-        if (row < TN && mm < p.M) cp_async_f32(&as_ring[slot][row], p.a_scale + hh * p.as_sb + mm * p.as_sm);
+        const int nn = pre.nt * kBlockN + row;
+        if (nn < p.N) cp_async_f32(&ws_ring[grp][slot][row], p.w_scale + pre.h * p.ws_sb + nn * p.ws_sn);
+        const int mm = pre.mt * TN + row;
+        if (row < TN && mm < p.M)
+          cp_async_f32(&as_ring[grp][slot][row], p.a_scale + pre.h * p.as_sb + mm * p.as_sm);
       }
       cp_async_commit();
+#pragma unroll
+      for (int e = 0; e < EG; ++e) pre.next(p.m_tiles, p.n_tiles);
     };
     if constexpr (kPrefetch) {
 #pragma unroll
-      for (int d = 0; d < kScaleRing - 1; ++d) issue_scales(tile + d, d);
+      for (int d = 0; d < kScaleRing - 1; ++d) issue_scales(tile + grp + EG * d, d);
     }
-    for (; g < g1; ++tile, kb0 = 0) {
+    for (; g < g1; ++tile, kb0 = 0, cur.next(p.m_tiles, p.n_tiles), ++seg) {
       const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
       const int kb1 = kb0 + static_cast<int>(seg_len);
       g += seg_len;
+      if (EG == 2 && (seg & 1) != grp) continue;  // the other group's segment
+      const int own = EG == 2 ? seg >> 1 : seg;   // index among this group's segments
       const bool whole = (kb0 == 0 && kb1 == KB);
-      const int c_first = whole ? 0 : p.sk.owner(tile * KB);
-      const int c_last = whole ? 0 : p.sk.owner((tile + 1) * KB - 1);
-      int h, nt, mt;
-      decode_tile(p, tile, h, nt, mt);
+      int c_first = 0, c_last = 0;
+      if (!whole) {
+        const long long cc = cut_contributors(p.sk.total, p.sk.grid, KB, tile);
+        c_first = static_cast<int>(cc & 0xffffffffLL);
+        c_last = static_cast<int>(cc >> 32);
+      }
+      const int h = cur.h, nt = cur.nt, mt = cur.mt;
       const int n = nt * kBlockN + row;
       const int m0 = mt * TN;
       // Scales of the rows this segment stores: copied into the ring
@@ -531,14 +565,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       float bias_pre = 0.0f;
       float as_pre[kPrefetch ? TN : 1];
       if constexpr (kPrefetch) {
-        const int slot = seg % kScaleRing;
+        const int slot = own % kScaleRing;
         cp_async_wait<kScaleRing - 2>();
-        named_bar_sync(1, 128);
-        issue_scales(tile + kScaleRing - 1, (seg + kScaleRing - 1) % kScaleRing);
+        named_bar_sync(ebar, 128);
+        issue_scales(tile + EG * (kScaleRing - 1), (own + kScaleRing - 1) % kScaleRing);
         if (!p.raw_f32) {
 #pragma unroll
-          for (int j = 0; j < TN; ++j) as_pre[j] = m0 + j < p.M ? as_ring[slot][j] : 1.0f;
-          if (n < p.N) ws_pre = ws_ring[slot][row];
+          for (int j4 = 0; j4 < TN / 4; ++j4) {
+            const float4 a4 = reinterpret_cast<const float4*>(as_ring[grp][slot])[j4];
+            as_pre[4 * j4 + 0] = m0 + 4 * j4 + 0 < p.M ? a4.x : 1.0f;
+            as_pre[4 * j4 + 1] = m0 + 4 * j4 + 1 < p.M ? a4.y : 1.0f;
+            as_pre[4 * j4 + 2] = m0 + 4 * j4 + 2 < p.M ? a4.z : 1.0f;
+            as_pre[4 * j4 + 3] = m0 + 4 * j4 + 3 < p.M ? a4.w : 1.0f;
+          }
+          if (n < p.N) ws_pre = ws_ring[grp][slot][row];
         } else {
 #pragma unroll
           for (int j = 0; j < TN; ++j) as_pre[j] = 1.0f;
@@ -562,13 +602,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool last = false;
       Acc other[kPrefetch ? TN : 1];
       if (!whole && is_first) {
-        if (threadIdx.x == 64)
-          sh_is_last =
+        if (threadIdx.x == leader)
+          sh_is_last[grp] =
               (p.sk.first_poll_ns && poll_counter(&p.counters[c_first], n_contrib - 1, abort_ptr, p.sk.first_poll_ns))
                   ? 1
                   : 0;
-        named_bar_sync(1, 128);
-        last = sh_is_last != 0;
+        named_bar_sync(ebar, 128);
+        last = sh_is_last[grp] != 0;
         if constexpr (kPrefetch) {
           if (last) {
 #pragma unroll
@@ -589,7 +629,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int acc = seg & (kNumAcc - 1);
       const uint32_t lane_addr = lane_addr0 + acc * kAccCols;
       const bool got = mbar_wait(&tfull_bar[acc], static_cast<uint32_t>((seg / kNumAcc) & 1), abort_ptr, p.status);
-      ++seg;
       const bool live = __all_sync(0xffffffffu, got);
       tc_fence_after();
       if (whole) {
@@ -610,7 +649,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 as16[j] = as_pre[c * 16 + j];
               }
               if (p.vec_out) {
-                uint16_t* stg = epi_stage + (warp - 2) * 512;
                 if (p.out_dtype == CB_DTYPE_BF16)
                   emit_chunk_vec<1, Acc>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
                 else
@@ -629,7 +667,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               Acc v[16];
 #pragma unroll
               for (int j = 0; j < 16; ++j) v[j] = acc_from_bits<Acc>(r[j]);
-              emit_row_any<TN, Acc>(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - 2) * 512);
+              emit_row_any<TN, Acc>(p, h, n, lane, m0, c * 16, v, stg);
             }
           }
         }
@@ -654,15 +692,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           __threadfence();
-          named_bar_sync(1, 128);
+          named_bar_sync(ebar, 128);
           if (is_first) {
             // the poll expired: last-arriver fallback, checked at once
-            if (threadIdx.x == 64)
-              sh_is_last = (!*abort_ptr && atomicAdd(&p.counters[c_first], 1) == n_contrib - 1) ? 1 : 0;
-            named_bar_sync(1, 128);
-            last = sh_is_last != 0;
+            if (threadIdx.x == leader)
+              sh_is_last[grp] = (!*abort_ptr && atomicAdd(&p.counters[c_first], 1) == n_contrib - 1) ? 1 : 0;
+            named_bar_sync(ebar, 128);
+            last = sh_is_last[grp] != 0;
             if (last) __threadfence();
-          } else if (threadIdx.x == 64 && !*abort_ptr) {
+          } else if (threadIdx.x == leader && !*abort_ptr) {
             // only a CTA's first segment can start inside a tile, so there is
             // at most one of these per CTA
             pend_old = atomicAdd(&p.counters[c_first], 1);
@@ -721,7 +759,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) as16[j] = as_pre[c * 16 + j];
               if (p.vec_out) {
-                uint16_t* stg = epi_stage + (warp - 2) * 512;
                 if (p.out_dtype == CB_DTYPE_BF16)
                   emit_chunk_vec<1, Acc>(p, h, n - lane, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
                 else
@@ -730,10 +767,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 emit_row_pre<Acc>(p, h, n, m0, c * 16, v, ws_pre, bias_pre, as16);
               }
             } else {
-              emit_row_any<TN, Acc>(p, h, n, lane, m0, c * 16, v, epi_stage + (warp - 2) * 512);
+              emit_row_any<TN, Acc>(p, h, n, lane, m0, c * 16, v, stg);
             }
           }
-          if (threadIdx.x == 64) p.counters[c_first] = 0;  // next launch starts from zero
+          if (threadIdx.x == leader) p.counters[c_first] = 0;  // next launch starts from zero
         }
         tc_fence_before();
         __syncwarp();
@@ -743,16 +780,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Deferred check of the part this CTA published without waiting: if its
     // bump was the tile's last arrival, the tile is reduced here, every part
     // (this CTA's included) read back from the partial slots.
-    if (threadIdx.x == 64) {
+    if (threadIdx.x == leader) {
       const int cf = pend_tile >= 0 ? p.sk.owner(pend_tile * KB) : 0;
       const int cl = pend_tile >= 0 ? p.sk.owner((pend_tile + 1) * KB - 1) : 0;
-      sh_is_last = (pend_tile >= 0 && !*abort_ptr && pend_old == cl - cf) ? 1 : 0;
-      sh_pend_tile = pend_tile;
+      sh_is_last[grp] = (pend_tile >= 0 && !*abort_ptr && pend_old == cl - cf) ? 1 : 0;
+      sh_pend_tile[grp] = pend_tile;
     }
-    named_bar_sync(1, 128);
-    if (sh_is_last) {
+    named_bar_sync(ebar, 128);
+    if (sh_is_last[grp]) {
       __threadfence();
-      const long long t = sh_pend_tile;
+      const long long t = sh_pend_tile[grp];
       const int cf = p.sk.owner(t * KB);
       const int cl = p.sk.owner((t + 1) * KB - 1);
       int h, nt, mt;
@@ -775,9 +812,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         part(cf, c, w);
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = w[j] + v[j];
-        emit_row_any<TN, Acc>(p, h, nt * kBlockN + row, lane, mt * TN, c * 16, v, epi_stage + (warp - 2) * 512);
+        emit_row_any<TN, Acc>(p, h, nt * kBlockN + row, lane, mt * TN, c * 16, v, stg);
       }
-      if (threadIdx.x == 64) p.counters[cf] = 0;  // next launch starts from zero
+      if (threadIdx.x == leader) p.counters[cf] = 0;  // next launch starts from zero
     }
   }
 
@@ -798,7 +835,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int TN, int KIND>
+template <int TN, int KIND, int EG>
 int launch_tn(const W8A8Launch& L, cudaStream_t stream, int grid, int stages, const Params& prm) {
   CUtensorMap tw, ta;
   int st = encode_tmap_3d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.w, static_cast<uint64_t>(L.K),
@@ -809,13 +846,13 @@ int launch_tn(const W8A8Launch& L, cudaStream_t stream, int grid, int stages, co
                       static_cast<uint64_t>(L.M), static_cast<uint64_t>(L.batch), L.aq_sm, L.aq_sb, kBlockK, TN,
                       CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != CB_OK) return st;
-  const size_t smem = static_cast<size_t>(stages) * (kWTileBytes + TN * kBlockK) + 4 * 1024 + 1024;
+  const size_t smem = static_cast<size_t>(stages) * (kWTileBytes + TN * kBlockK) + EG * 4 * 1024 + 1024;
   static thread_local int configured_dev = -1;
   static thread_local size_t configured_smem = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_dev != dev || configured_smem < smem) {
-    cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_kernel<TN, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_kernel<TN, KIND, EG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return CB_ERR_CUDA;
     configured_dev = dev;
@@ -823,7 +860,7 @@ int launch_tn(const W8A8Launch& L, cudaStream_t stream, int grid, int stages, co
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads_for(EG));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -831,22 +868,25 @@ int launch_tn(const W8A8Launch& L, cudaStream_t stream, int grid, int stages, co
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, w8a8_gemm_kernel<TN, KIND>, tw, ta, prm));
+  return cuda_status(cudaLaunchKernelEx(&cfg, w8a8_gemm_kernel<TN, KIND, EG>, tw, ta, prm));
 }
 
 template <int KIND>
 int dispatch_tn(const W8A8Launch& L, cudaStream_t stream, int TN, int grid, int stages, const Params& p) {
+  const bool two_groups = p.kb_per_tile <= kMaxKbTwoGroups;
   switch (TN) {
     case 16:
-      return launch_tn<16, KIND>(L, stream, grid, stages, p);
+      return two_groups ? launch_tn<16, KIND, 2>(L, stream, grid, stages, p)
+                        : launch_tn<16, KIND, 1>(L, stream, grid, stages, p);
     case 32:
-      return launch_tn<32, KIND>(L, stream, grid, stages, p);
+      return two_groups ? launch_tn<32, KIND, 2>(L, stream, grid, stages, p)
+                        : launch_tn<32, KIND, 1>(L, stream, grid, stages, p);
     case 64:
-      return launch_tn<64, KIND>(L, stream, grid, stages, p);
+      return launch_tn<64, KIND, 1>(L, stream, grid, stages, p);
     case 128:
-      return launch_tn<128, KIND>(L, stream, grid, stages, p);
+      return launch_tn<128, KIND, 1>(L, stream, grid, stages, p);
     default:
-      return launch_tn<256, KIND>(L, stream, grid, stages, p);
+      return launch_tn<256, KIND, 1>(L, stream, grid, stages, p);
   }
 }
 
