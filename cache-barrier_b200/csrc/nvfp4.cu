@@ -482,8 +482,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int kb1 = kb0 + static_cast<int>(seg_len);
       g += seg_len;
       const bool whole = (kb0 == 0 && kb1 == KB);
-      const int c_first = whole ? 0 : p.sk.owner(tile * KB);
-      const int c_last = whole ? 0 : p.sk.owner((tile + 1) * KB - 1);
+      int c_first = 0, c_last = 0;
+      if (!whole) {
+        const long long cc = cut_contributors(p.sk.total, p.sk.grid, KB, tile);
+        c_first = static_cast<int>(cc & 0xffffffffLL);
+        c_last = static_cast<int>(cc >> 32);
+      }
       const int n_contrib = c_last - c_first + 1;
       const bool is_first = static_cast<int>(blockIdx.x) == c_first;
       int nt, mt;

@@ -168,13 +168,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kBoxBytes = TN * 128;
   constexpr uint32_t kStageBytes = kWTileBytes + kATileBytes;
   constexpr uint32_t kAccCols = TN < 32 ? 32 : TN;
-  constexpr uint32_t kTmemCols = 2 * kAccCols;
+  // Accumulator ring in TMEM (the A operand lives in shared memory): segment s
+  // uses accumulator s % kNumAcc, so with short K (one k-block per tile) the
+  // MMAs run up to kNumAcc - 1 tiles ahead of the epilogue.
+  constexpr int kNumAcc = static_cast<int>(512 / kAccCols) < 8 ? static_cast<int>(512 / kAccCols) : 8;
+  constexpr uint32_t kTmemCols = kNumAcc * kAccCols;
+  static_assert((kNumAcc & (kNumAcc - 1)) == 0 && kTmemCols <= 512, "accumulator ring must fit TMEM");
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
   __shared__ __align__(8) uint64_t aempty_bar[kNumABuf];
-  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], drain_bar;  // accumulators double-buffered
+  __shared__ __align__(8) uint64_t tfull_bar[kNumAcc], tempty_bar[kNumAcc], drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   __shared__ long long sh_pend_tile;
@@ -204,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty_bar[s], 5);  // 4 dequant warps + 1 MMA commit
     }
     for (int b = 0; b < kNumABuf; ++b) mbar_init(&aempty_bar[b], 1);
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kNumAcc; ++a) {
       mbar_init(&tfull_bar[a], 1);
       mbar_init(&tempty_bar[a], 4);
     }
@@ -295,12 +300,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long long seg_len = (KB - kb_first) < (g1 - g) ? (KB - kb_first) : (g1 - g);
       const long long seg_end = g + seg_len;
       kb_first = 0;
-      // segment `seg` accumulates into accumulator seg % 2, free once the
-      // epilogue drained the segment two back
-      const int acc = seg & 1;
+      // segment `seg` accumulates into accumulator seg % kNumAcc, free once the
+      // epilogue drained the segment kNumAcc back
+      const int acc = seg & (kNumAcc - 1);
       const uint32_t tmem_d = tmem_base + acc * kAccCols;
       if (lane == 0 && !bad)
-        bad = !mbar_wait(&tempty_bar[acc], static_cast<uint32_t>(((seg >> 1) & 1) ^ 1), abort_ptr, p.status);
+        bad = !mbar_wait(&tempty_bar[acc], static_cast<uint32_t>(((seg / kNumAcc) & 1) ^ 1), abort_ptr, p.status);
       for (bool first = true; g < seg_end; ++g, first = false) {
         const int j = static_cast<int>(g - g0);
         const int b = j % kNumABuf;
@@ -345,8 +350,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ja = consumed - 1 - (lane - 24);  // lanes 24.. : A-buffer releases
       if (lane >= 24 && lane < 24 + kNumABuf && ja >= 0)
         mbar_wait(&aempty_bar[ja % kNumABuf], static_cast<uint32_t>((ja / kNumABuf) & 1), nullptr, p.status);
-      const int t = n_tfull - 1 - (lane - 30);  // lanes 30, 31: the last two accumulator hand-offs
-      if (lane >= 30 && t >= 0) mbar_wait(&tfull_bar[t & 1], static_cast<uint32_t>((t >> 1) & 1), nullptr, p.status);
+      const int t = n_tfull - 1 - (lane - 16);  // lanes 16.. : the last kNumAcc accumulator hand-offs
+      if (lane >= 16 && lane < 16 + kNumAcc && t >= 0)
+        mbar_wait(&tfull_bar[t & (kNumAcc - 1)], static_cast<uint32_t>((t / kNumAcc) & 1), nullptr, p.status);
     }
     __syncwarp();
   } else if (warp < kEpiWarp0) {
@@ -357,7 +363,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int grp = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;  // TMEM lanes of this warp
     const typename Dq<T>::T2 bias = Dq<T>::bias();
     const bool fold_scale = !p.scale_in_epilogue;
     pdl_wait_primary();
@@ -366,11 +371,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     int kb0 = static_cast<int>(g0 - tile * KB);
     int s_next = 0;  // ring stage and phase of k-block j, advanced per k-block
     uint32_t ph_next = 0;
-    for (; g < g1; ++tile, kb0 = 0) {
+    TileCursor cur;  // (batch, n-tile, m-tile) of the segment's tile, advanced without division
+    cur.seek(tile, p.m_tiles, p.n_tiles);
+    for (; g < g1; ++tile, kb0 = 0, cur.next(p.m_tiles, p.n_tiles)) {
       const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
       const int kb1 = kb0 + static_cast<int>(seg_len);
-      int h, nt, mt;
-      decode_tile(p, tile, h, nt, mt);
+      const int h = cur.h, nt = cur.nt;
       const int n = nt * kBlockN + row;
       // Group scales are prefetched one k-block of this group ahead (a group
       // takes every fourth k-block), so their global-load latency is off the
@@ -464,17 +470,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     int kb0 = static_cast<int>(g0 - tile * KB);
     int pend_old = -1;         // kEpiThread0: counter value its deferred bump returned
     long long pend_tile = -1;  // kEpiThread0: tile of that bump (-1: none)
-    for (int seg = 0; g < g1; ++tile, kb0 = 0, ++seg) {
+    TileCursor cur;  // (batch, n-tile, m-tile) of the segment's tile, advanced without division
+    cur.seek(tile, p.m_tiles, p.n_tiles);
+    for (int seg = 0; g < g1; ++tile, kb0 = 0, ++seg, cur.next(p.m_tiles, p.n_tiles)) {
       const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
       const int kb1 = kb0 + static_cast<int>(seg_len);
       g += seg_len;
-      int h, nt, mt;
-      decode_tile(p, tile, h, nt, mt);
+      const int h = cur.h, nt = cur.nt, mt = cur.mt;
       const int n = nt * kBlockN + row;
-      const int acc = seg & 1;
+      const int acc = seg & (kNumAcc - 1);
       const bool whole = (kb0 == 0 && kb1 == KB);
-      const int c_first = whole ? 0 : p.sk.owner(tile * KB);
-      const int c_last = whole ? 0 : p.sk.owner((tile + 1) * KB - 1);
+      int c_first = 0, c_last = 0;
+      if (!whole) {
+        const long long cc = cut_contributors(p.sk.total, p.sk.grid, KB, tile);
+        c_first = static_cast<int>(cc & 0xffffffffLL);
+        c_last = static_cast<int>(cc >> 32);
+      }
       const int n_contrib = c_last - c_first + 1;
       const bool is_first = static_cast<int>(blockIdx.x) == c_first;
       constexpr bool kPrefetch = TN <= 32;
@@ -517,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      const bool got = mbar_wait(&tfull_bar[acc], static_cast<uint32_t>((seg >> 1) & 1), abort_ptr, p.status);
+      const bool got = mbar_wait(&tfull_bar[acc], static_cast<uint32_t>((seg / kNumAcc) & 1), abort_ptr, p.status);
       const bool live = __all_sync(0xffffffffu, got);
       tc_fence_after();
       const int m0 = mt * TN;
