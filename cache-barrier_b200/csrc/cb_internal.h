@@ -54,12 +54,16 @@ inline size_t workspace_need(int grid, size_t slot_bytes) {
   return kWsHeader + kWsCounters + 2 * static_cast<size_t>(grid) * slot_bytes;
 }
 
-// Stream-K grid: one CTA per SM, but at least TN / 16 k-blocks per CTA, so wide
-// token tiles are not cut into many small ranges (every cut tile is summed by
-// one CTA from TN * 128 * 4-byte partials of all its contributors).
-inline int stream_k_grid(long long total_kb, int sms, int TN, int min_kb_per_cta = 1) {
+// Stream-K grid: one CTA per SM, but at least TN / 16 (and min_kb_per_cta)
+// k-blocks per CTA, so wide token tiles are not cut into many small ranges
+// (every cut tile is summed by one CTA from TN * 128 * 4-byte partials of all
+// its contributors). Neither minimum exceeds the k-blocks of one tile: a range
+// of whole tiles cuts nothing, and with short K (one k-block per tile) every
+// SM then gets tiles.
+inline int stream_k_grid(long long total_kb, int sms, int TN, int kb_per_tile, int min_kb_per_cta = 1) {
   long long per_cta = TN >= 32 ? TN / 16 : 1;
   if (per_cta < min_kb_per_cta) per_cta = min_kb_per_cta;
+  if (per_cta > kb_per_tile) per_cta = kb_per_tile;
   long long grid = (total_kb + per_cta - 1) / per_cta;
   const int max_grid = sms < kMaxGrid ? sms : kMaxGrid;
   if (grid > max_grid) grid = max_grid;

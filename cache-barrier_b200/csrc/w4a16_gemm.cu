@@ -777,7 +777,7 @@ int launch_w4a16(const W4A16Launch& L, cudaStream_t stream) {
   const long long total = tiles * p.kb_per_tile;
   const int sms = sm_count();
   if (sms <= 0) return CB_ERR_CUDA;
-  const int grid = stream_k_grid(total, sms, TN);
+  const int grid = stream_k_grid(total, sms, TN, p.kb_per_tile);
   const size_t need = workspace_need(grid, static_cast<size_t>(TN) * kBlockN * sizeof(float));
   if (L.workspace == nullptr || L.workspace_bytes < need) return CB_ERR_WORKSPACE;
   const size_t stage_bytes = kWTileBytes + static_cast<size_t>(TN) * kBlockK * 2;

@@ -917,7 +917,7 @@ int launch_w8a8(const W8A8Launch& L, cudaStream_t stream) {
   const long long total = tiles * p.kb_per_tile;
   int sms = sm_count();
   if (sms <= 0) return CB_ERR_CUDA;
-  const int grid = stream_k_grid(total, sms, TN, kMinKbPerCta);
+  const int grid = stream_k_grid(total, sms, TN, p.kb_per_tile, kMinKbPerCta);
   const size_t need = workspace_need(grid, static_cast<size_t>(TN) * kBlockN * sizeof(int32_t));
   if (L.workspace == nullptr || L.workspace_bytes < need) return CB_ERR_WORKSPACE;
   // Ring depth: as many stages as ~200 KiB of shared memory holds.
