@@ -30,6 +30,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", choices=["w8a8", "w8a8_dynamic", "w4a16", "nvfp4", "mla"], default="w8a8")
     ap.add_argument("--heads", type=int, default=16, help="mla: batch of heads (latents [heads, tokens, k])")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="w8a8: batch of GEMMs (the reference's gate shapes: --batch 128 --k 128 --n 32*W)")
     ap.add_argument("--tokens", type=int, default=32)
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192)
@@ -44,8 +46,13 @@ def main():
     a = torch.randn(T, K, generator=g, device=dev).to(torch.bfloat16)
     out = torch.empty(T, N, dtype=torch.bfloat16, device=dev)
     if args.op.startswith("w8a8"):
-        ws_ = ((torch.randn(N, generator=g, device=dev) * 0.01).abs() + 1e-4).float()
-        weights = [ops.repack_w8_kmajor(torch.randint(-127, 128, (K, N), generator=g, dtype=torch.int8, device=dev))
+        Hb = args.batch
+        if Hb > 1:
+            a = torch.randn(Hb, T, K, generator=g, device=dev).to(torch.bfloat16)
+            out = torch.empty(Hb, T, N, dtype=torch.bfloat16, device=dev)
+        wshape = (Hb, K, N) if Hb > 1 else (K, N)
+        ws_ = ((torch.randn(*wshape[:-2], N, generator=g, device=dev) * 0.01).abs() + 1e-4).float()
+        weights = [ops.repack_w8_kmajor(torch.randint(-127, 128, wshape, generator=g, dtype=torch.int8, device=dev))
                    for _ in range(args.copies)]
         q, s = ops.quant_act_i8(a)
 
