@@ -209,6 +209,22 @@ __device__ __forceinline__ void emit_chunk_vec(const Params& p, int h, int n_war
   __syncwarp();
 }
 
+// Warp-collective store of one 16-token chunk with its scales at hand (from
+// registers or the shared-memory scale ring): the vector path for 16-bit
+// outputs, else element stores. Same arithmetic and rounding as emit_row.
+template <typename Acc>
+__device__ __forceinline__ void emit_pre(const Params& p, int h, int n, int lane, int m0, int t0, const Acc (&v)[16],
+                                         float ws, float bv, const float (&as)[16], uint16_t* stg) {
+  if (p.vec_out) {
+    if (p.out_dtype == CB_DTYPE_BF16)
+      emit_chunk_vec<1, Acc>(p, h, n - lane, lane, m0, t0, v, ws, bv, as, stg);
+    else
+      emit_chunk_vec<0, Acc>(p, h, n - lane, lane, m0, t0, v, ws, bv, as, stg);
+  } else {
+    emit_row_pre<Acc>(p, h, n, m0, t0, v, ws, bv, as);
+  }
+}
+
 // Warp-collective store of one 16-token chunk for the paths without preloaded
 // scales (token tiles above 32): loads the scales as emit_row does, then takes
 // the vector path for 16-bit outputs.
@@ -282,7 +298,7 @@ __global__ void __launch_bounds__(threads_for(EG), 1)
   __shared__ int sh_is_last[2];  // per epilogue group: whether this CTA reduces the cut tile at hand
   // scales of the next kScaleRing segments (epilogue, token tiles up to 32)
   __shared__ __align__(16) float ws_ring[EG][kScaleRing][kBlockN];
-  __shared__ __align__(16) float as_ring[EG][kScaleRing][TN <= 32 ? TN : 4];
+  __shared__ __align__(16) float as_ring[EG][kScaleRing][TN];
   volatile int* abort_ptr = &abort_flag;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -514,7 +530,10 @@ __global__ void __launch_bounds__(threads_for(EG), 1)
     int kb0 = static_cast<int>(g0 - tile * KB);
     int pend_old = -1;         // leader: counter value its deferred bump returned
     long long pend_tile = -1;  // leader: tile of that bump (-1: none)
-    constexpr bool kPrefetch = TN <= 32;
+    constexpr bool kPrefetch = TN <= 32;  // token scales in registers
+    // the first contributor of a cut tile sums the others' parts into registers
+    // while its own last MMAs run
+    constexpr bool kPrefetchParts = TN <= 64;
     const long long last_tile = (g1 - 1) / KB;
     // Copies (cp.async, one commit group per own segment) of the scales of the
     // group's k-th own segment into its ring slot k % kScaleRing: each thread
@@ -530,18 +549,18 @@ __global__ void __launch_bounds__(threads_for(EG), 1)
       if (t <= last_tile && !p.raw_f32) {
         const int nn = pre.nt * kBlockN + row;
         if (nn < p.N) cp_async_f32(&ws_ring[grp][slot][row], p.w_scale + pre.h * p.ws_sb + nn * p.ws_sn);
-        const int mm = pre.mt * TN + row;
-        if (row < TN && mm < p.M)
-          cp_async_f32(&as_ring[grp][slot][row], p.a_scale + pre.h * p.as_sb + mm * p.as_sm);
+#pragma unroll
+        for (int r = row; r < TN; r += kBlockN) {
+          const int mm = pre.mt * TN + r;
+          if (mm < p.M) cp_async_f32(&as_ring[grp][slot][r], p.a_scale + pre.h * p.as_sb + mm * p.as_sm);
+        }
       }
       cp_async_commit();
 #pragma unroll
       for (int e = 0; e < EG; ++e) pre.next(p.m_tiles, p.n_tiles);
     };
-    if constexpr (kPrefetch) {
 #pragma unroll
-      for (int d = 0; d < kScaleRing - 1; ++d) issue_scales(tile + grp + EG * d, d);
-    }
+    for (int d = 0; d < kScaleRing - 1; ++d) issue_scales(tile + grp + EG * d, d);
     for (; g < g1; ++tile, kb0 = 0, cur.next(p.m_tiles, p.n_tiles), ++seg) {
       const long long seg_len = (KB - kb0) < (g1 - g) ? (KB - kb0) : (g1 - g);
       const int kb1 = kb0 + static_cast<int>(seg_len);
@@ -561,14 +580,22 @@ __global__ void __launch_bounds__(threads_for(EG), 1)
       // Scales of the rows this segment stores: copied into the ring
       // kScaleRing - 1 segments ago; wait for this segment's group, make every
       // thread's copies visible, then reuse the slot the previous segment read.
+      // Token tiles up to 32 keep their token scales in registers; wider ones
+      // read them from the ring slot per 16-token chunk (scales16).
       float ws_pre = 1.0f;
       float bias_pre = 0.0f;
       float as_pre[kPrefetch ? TN : 1];
+      const int slot = own % kScaleRing;
+      cp_async_wait<kScaleRing - 2>();
+      named_bar_sync(ebar, 128);
+      issue_scales(tile + EG * (kScaleRing - 1), (own + kScaleRing - 1) % kScaleRing);
+      if (!p.raw_f32 && n < p.N) ws_pre = ws_ring[grp][slot][row];
+      if (p.bias && n < p.N) bias_pre = load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n);
+      auto scales16 = [&](int c, float (&as16)[16]) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) as16[j] = (!p.raw_f32 && m0 + c * 16 + j < p.M) ? as_ring[grp][slot][c * 16 + j] : 1.0f;
+      };
       if constexpr (kPrefetch) {
-        const int slot = own % kScaleRing;
-        cp_async_wait<kScaleRing - 2>();
-        named_bar_sync(ebar, 128);
-        issue_scales(tile + EG * (kScaleRing - 1), (own + kScaleRing - 1) % kScaleRing);
         if (!p.raw_f32) {
 #pragma unroll
           for (int j4 = 0; j4 < TN / 4; ++j4) {
@@ -578,12 +605,10 @@ __global__ void __launch_bounds__(threads_for(EG), 1)
             as_pre[4 * j4 + 2] = m0 + 4 * j4 + 2 < p.M ? a4.z : 1.0f;
             as_pre[4 * j4 + 3] = m0 + 4 * j4 + 3 < p.M ? a4.w : 1.0f;
           }
-          if (n < p.N) ws_pre = ws_ring[grp][slot][row];
         } else {
 #pragma unroll
           for (int j = 0; j < TN; ++j) as_pre[j] = 1.0f;
         }
-        if (p.bias && n < p.N) bias_pre = load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n);
       }
       // Cut tile. Its first contributor (whose range ends in this tile; the
       // others covered it at the start of theirs, so they are done first when
@@ -600,7 +625,7 @@ __global__ void __launch_bounds__(threads_for(EG), 1)
       const int n_contrib = c_last - c_first + 1;
       const bool is_first = static_cast<int>(blockIdx.x) == c_first;
       bool last = false;
-      Acc other[kPrefetch ? TN : 1];
+      Acc other[kPrefetchParts ? TN : 1];
       if (!whole && is_first) {
         if (threadIdx.x == leader)
           sh_is_last[grp] =
@@ -609,7 +634,7 @@ __global__ void __launch_bounds__(threads_for(EG), 1)
                   : 0;
         named_bar_sync(ebar, 128);
         last = sh_is_last[grp] != 0;
-        if constexpr (kPrefetch) {
+        if constexpr (kPrefetchParts) {
           if (last) {
 #pragma unroll
             for (int c = 0; c < TN / 16; ++c) {
@@ -665,9 +690,11 @@ __global__ void __launch_bounds__(threads_for(EG), 1)
               tmem_ld16(lane_addr + c * 16, r);
               tmem_ld_wait();
               Acc v[16];
+              float as16[16];
 #pragma unroll
               for (int j = 0; j < 16; ++j) v[j] = acc_from_bits<Acc>(r[j]);
-              emit_row_any<TN, Acc>(p, h, n, lane, m0, c * 16, v, stg);
+              scales16(c, as16);
+              emit_pre<Acc>(p, h, n, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
             }
           }
         }
@@ -675,7 +702,7 @@ __global__ void __launch_bounds__(threads_for(EG), 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       } else {
-        const bool prefetched = kPrefetch && last && is_first;
+        const bool prefetched = kPrefetchParts && last && is_first;
         if (!last) {
           // publish this CTA's part (raw accumulator bits) and count it
           const int slot = static_cast<int>(blockIdx.x) * 2 + p.sk.kind(blockIdx.x, tile);
@@ -716,7 +743,7 @@ __global__ void __launch_bounds__(threads_for(EG), 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = __ldcg(src + j * kBlockN);
           };
-#pragma unroll(kPrefetch ? 2 : 1)
+#pragma unroll(kPrefetchParts ? TN / 16 : 1)
           for (int c = 0; c < TN / 16; ++c) {
             uint32_t r[16];
             __syncwarp();
@@ -727,7 +754,7 @@ __global__ void __launch_bounds__(threads_for(EG), 1)
             for (int j = 0; j < 16; ++j) own[j] = acc_from_bits<Acc>(r[j]);
             // S = left fold of the parts of c_first + 1 .. c_last
             if (prefetched) {
-              if constexpr (kPrefetch) {
+              if constexpr (kPrefetchParts) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] = other[c * 16 + j];
               }
@@ -767,7 +794,9 @@ __global__ void __launch_bounds__(threads_for(EG), 1)
                 emit_row_pre<Acc>(p, h, n, m0, c * 16, v, ws_pre, bias_pre, as16);
               }
             } else {
-              emit_row_any<TN, Acc>(p, h, n, lane, m0, c * 16, v, stg);
+              float as16[16];
+              scales16(c, as16);
+              emit_pre<Acc>(p, h, n, lane, m0, c * 16, v, ws_pre, bias_pre, as16, stg);
             }
           }
           if (threadIdx.x == leader) p.counters[c_first] = 0;  // next launch starts from zero

@@ -23,6 +23,9 @@ SHAPES = [  # (B, M, N, K)
     (1, 256, 256, 1024),
     (1, 300, 384, 512),
     (128, 1, 512, 128),
+    (64, 32, 512, 128),    # short K: one k-block per tile, two epilogue groups
+    (16, 20, 1024, 256),   # two k-blocks per tile
+    (1, 64, 1280, 2560),   # 64-token tiles with scales from the shared-memory ring, cut tiles
     (1, 8, 8192, 8192),
 ]
 
