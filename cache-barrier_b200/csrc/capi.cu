@@ -169,17 +169,49 @@ __global__ void unpack_rows_i4_kernel(const uint8_t* __restrict__ src, long long
   }
 }
 
-// Unpack B [K/2, N] (k-packed along rows) to 8-bit K-major [N, K].
-__global__ void unpack_cols_i4_kernel(const uint8_t* __restrict__ src, long long ld, uint8_t* __restrict__ dst,
-                                      long long K, long long N, int wrap) {
+// Unpack B [K/2, N] (k-packed along rows) to 8-bit K-major [N, K] through
+// shared memory, one CTA per 64 (packed k-pairs) x 64 (n) tile (1-D grid, n
+// tiles fastest): source rows are read as 64 contiguous bytes per row and each
+// destination row is written as 128 contiguous bytes, 32 per thread in two
+// 16-byte stores, so both sides are coalesced. Requires K % 32 == 0 (checked by
+// the caller) and a 16-byte aligned dst.
+constexpr int kUnpackTile = 64;
+__global__ void __launch_bounds__(256) unpack_cols_i4_tiled_kernel(const uint8_t* __restrict__ src, long long ld,
+                                                                   uint8_t* __restrict__ dst, long long K, long long N,
+                                                                   int wrap) {
+  __shared__ __align__(16) uint8_t tile[kUnpackTile][kUnpackTile + 16];  // [k-pair][n], rows 16-byte aligned
   const long long half = K / 2;
-  const long long total = half * N;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long n = i / half, c = i % half;  // consecutive threads walk k for one n
-    const uint8_t byte = src[c * ld + n];
-    dst[n * K + 2 * c] = nibble_value(byte & 0xF, wrap);
-    dst[n * K + 2 * c + 1] = nibble_value(byte >> 4, wrap);
+  const long long n_tiles = (N + kUnpackTile - 1) / kUnpackTile;
+  const long long c0 = (blockIdx.x / n_tiles) * kUnpackTile;
+  const long long n0 = (blockIdx.x % n_tiles) * kUnpackTile;
+  {
+    const int r = threadIdx.x >> 2, q = threadIdx.x & 3;  // row r, bytes 16q..16q+15 of the tile row
+    const long long c = c0 + r;
+    const long long nb = n0 + q * 16;
+    const uint8_t* sp = src + c * ld + nb;
+    if (c < half && nb + 16 <= N && (reinterpret_cast<uintptr_t>(sp) & 15u) == 0) {
+      *reinterpret_cast<uint4*>(&tile[r][q * 16]) = *reinterpret_cast<const uint4*>(sp);
+    } else {
+#pragma unroll
+      for (int b = 0; b < 16; ++b) tile[r][q * 16 + b] = (c < half && nb + b < N) ? sp[b] : 0;
+    }
+  }
+  __syncthreads();
+  const int nn = threadIdx.x >> 2, q = threadIdx.x & 3;  // destination row n0 + nn, k-pairs 16q..16q+15
+  const long long n = n0 + nn;
+  const long long cq = c0 + q * 16;
+  if (n < N && cq < half) {  // half % 16 == 0: the thread's 16 k-pairs are all in range
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint8_t b0 = tile[q * 16 + 2 * i][nn], b1 = tile[q * 16 + 2 * i + 1][nn];
+      w[i] = static_cast<uint32_t>(nibble_value(b0 & 0xF, wrap)) | (static_cast<uint32_t>(nibble_value(b0 >> 4, wrap)) << 8) |
+             (static_cast<uint32_t>(nibble_value(b1 & 0xF, wrap)) << 16) |
+             (static_cast<uint32_t>(nibble_value(b1 >> 4, wrap)) << 24);
+    }
+    uint4* d = reinterpret_cast<uint4*>(dst + n * K + 2 * cq);
+    d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d[1] = make_uint4(w[4], w[5], w[6], w[7]);
   }
 }
 
@@ -551,7 +583,11 @@ int cb_w4a4_gemm(const uint8_t* a_packed, const uint8_t* b_packed, float* c, int
   uint8_t* a8 = static_cast<uint8_t*>(workspace) + gemm_bytes;
   uint8_t* b8 = a8 + align_up(static_cast<size_t>(M) * K, 256);
   unpack_rows_i4_kernel<<<grid_for(M * K / 2, 256), 256, 0, s>>>(a_packed, lda, a8, M, K, wrap);
-  unpack_cols_i4_kernel<<<grid_for(N * K / 2, 256), 256, 0, s>>>(b_packed, ldb, b8, K, N, wrap);
+  {
+    const long long tiles = ((N + kUnpackTile - 1) / kUnpackTile) * ((K / 2 + kUnpackTile - 1) / kUnpackTile);
+    if (tiles > 0x7fffffffLL) return CB_ERR_TOO_LARGE;
+    unpack_cols_i4_tiled_kernel<<<static_cast<unsigned>(tiles), 256, 0, s>>>(b_packed, ldb, b8, K, N, wrap);
+  }
   if (cudaGetLastError() != cudaSuccess) return CB_ERR_CUDA;
   W8A8Launch L = {};
   L.aq = reinterpret_cast<const int8_t*>(a8);
