@@ -102,6 +102,69 @@ __global__ void __launch_bounds__(kThreads) act_quant_kernel(const T* __restrict
   if (threadIdx.x == 0) scale[b * s_sb + m] = s;
 }
 
+// Long rows held in registers: one CTA of kRegThreads threads per row loads the
+// whole row at once (NV 16-byte vectors per thread, all in flight together),
+// reduces the amax and quantizes from the same registers, so a row costs one
+// memory round trip instead of a loop of dependent loads and a second pass
+// over the row. Same arithmetic as act_quant_kernel (the maximum does not
+// depend on the order of the elements).
+constexpr int kRegThreads = 512;
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kRegThreads) act_quant_reg_kernel(const T* __restrict__ a, long long a_sb,
+                                                                     long long a_sm, int8_t* __restrict__ q,
+                                                                     long long q_sb, long long q_sm,
+                                                                     float* __restrict__ scale, long long s_sb, int M,
+                                                                     int K) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  __shared__ float red[kRegThreads / 32];
+  const int row = blockIdx.x;
+  const int b = row / M, m = row % M;
+  const uint4* av = reinterpret_cast<const uint4*>(a + b * a_sb + m * a_sm);
+  uint2* qv = reinterpret_cast<uint2*>(q + b * q_sb + m * q_sm);
+  const int nvec = K / 8;
+  uint4 u[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int idx = threadIdx.x + i * kRegThreads;
+    if (idx < nvec) u[i] = av[idx];
+  }
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (threadIdx.x + i * kRegThreads < nvec) {
+      const T* e = reinterpret_cast<const T*>(&u[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(to_f32(e[j])));
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = amax;
+  __syncthreads();
+  if (warp == 0) {
+    float v = lane < kRegThreads / 32 ? red[lane] : 0.0f;
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float s = fmaxf(__fdiv_rn(red[0], 127.0f), 1e-8f);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int idx = threadIdx.x + i * kRegThreads;
+    if (idx < nvec) {
+      const T* e = reinterpret_cast<const T*>(&u[i]);
+      uint2 o;
+      int8_t* ob = reinterpret_cast<int8_t*>(&o);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ob[j] = quant1(to_f32(e[j]), s);
+      qv[idx] = o;
+    }
+  }
+  if (threadIdx.x == 0) scale[b * s_sb + m] = s;
+}
+
 // Short rows (K <= kWarpRowMaxK), many of them (a batch of heads x tokens): one
 // warp per row, kThreads / 32 rows per CTA, the same arithmetic as
 // act_quant_kernel. A CTA per row would spend its time launching.
@@ -298,6 +361,28 @@ int launch_act_quant(const void* a, int a_dtype, int64_t batch, int64_t M, int64
                              static_cast<long long>(s_sb), Mi, Ki, rows);
     else
       return CB_ERR_DTYPE;
+    return cuda_status(e);
+  }
+  if (vec_ok && K / 8 <= 8 * kRegThreads) {
+    // whole row in registers: NV vectors per thread, the smallest of 2, 4, 8 that holds it
+    cfg.blockDim = dim3(kRegThreads);
+    const int nvec = static_cast<int>(K / 8);
+    const bool bf = a_dtype == CB_DTYPE_BF16;
+    if (!bf && a_dtype != CB_DTYPE_F16) return CB_ERR_DTYPE;
+#define CB_ACTQ_REG(NV)                                                                                            \
+  (bf ? cudaLaunchKernelEx(&cfg, act_quant_reg_kernel<__nv_bfloat16, NV>, static_cast<const __nv_bfloat16*>(a),    \
+                           static_cast<long long>(a_sb), static_cast<long long>(a_sm), q, static_cast<long long>(q_sb), \
+                           static_cast<long long>(q_sm), scale, static_cast<long long>(s_sb), Mi, Ki)                  \
+      : cudaLaunchKernelEx(&cfg, act_quant_reg_kernel<__half, NV>, static_cast<const __half*>(a),                  \
+                           static_cast<long long>(a_sb), static_cast<long long>(a_sm), q, static_cast<long long>(q_sb), \
+                           static_cast<long long>(q_sm), scale, static_cast<long long>(s_sb), Mi, Ki))
+    if (nvec <= 2 * kRegThreads)
+      e = CB_ACTQ_REG(2);
+    else if (nvec <= 4 * kRegThreads)
+      e = CB_ACTQ_REG(4);
+    else
+      e = CB_ACTQ_REG(8);
+#undef CB_ACTQ_REG
     return cuda_status(e);
   }
   if (a_dtype == CB_DTYPE_BF16) {
