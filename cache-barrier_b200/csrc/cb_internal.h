@@ -151,6 +151,12 @@ int launch_w4a16(const W4A16Launch& L, cudaStream_t stream);
 bool w4a16_resident_eligible(const W4A16Launch& L);
 int launch_w4a16_resident(const W4A16Launch& L, cudaStream_t stream);
 size_t w4a16_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K);
+// One to four tokens: the dp4a GEMV kernel (w4a16_gemv.cu) instead of the
+// tensor-core kernel; at most kGemvCtasPerSm CTAs per SM when it splits K.
+constexpr int kGemvMaxTokens = 4;
+constexpr int kGemvCtasPerSm = 4;
+bool w4a16_gemv_eligible(const W4A16Launch& L);
+int launch_w4a16_gemv(const W4A16Launch& L, cudaStream_t stream);
 
 // NVFP4 GEMM: out[M, N] = alpha * A[M, K] . B[N, K]^T (nvfp4.cu). a/b: packed
 // e2m1 [rows, K/2] with row strides a_sm / b_sn in bytes; a_sf / b_sf: swizzled

@@ -755,13 +755,20 @@ size_t w4a16_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K) {
   (void)K;
   int sms = sm_count();
   if (sms <= 0) sms = 148;
-  return workspace_need(sms, static_cast<size_t>(token_tile(M, kMaxTokenTile)) * kBlockN * sizeof(float));
+  const size_t tc = workspace_need(sms, static_cast<size_t>(token_tile(M, kMaxTokenTile)) * kBlockN * sizeof(float));
+  // the dp4a path for up to kGemvMaxTokens tokens: at most kGemvCtasPerSm CTAs per SM
+  const size_t gv = workspace_need(kGemvCtasPerSm * sms, static_cast<size_t>(kGemvMaxTokens) * kBlockN * sizeof(float));
+  return tc > gv ? tc : gv;
 }
 
 int launch_w4a16(const W4A16Launch& L, cudaStream_t stream) {
   if (L.batch == 0 || L.M == 0 || L.N == 0) return CB_OK;
   if (w4a16_resident_eligible(L)) {
     const int st = launch_w4a16_resident(L, stream);
+    if (st != CB_ERR_UNSUPPORTED) return st;
+  }
+  if (w4a16_gemv_eligible(L)) {
+    const int st = launch_w4a16_gemv(L, stream);
     if (st != CB_ERR_UNSUPPORTED) return st;
   }
   const int TN = token_tile(L.M, kMaxTokenTile);

@@ -47,6 +47,10 @@ SHAPES_G128 = [  # (B, M, N, K)
     (4, 1, 512, 128),
     (16, 512, 128, 512),
     (1, 32, 8192, 8192),
+    # one to four tokens take the dp4a GEMV kernel: ragged K and N, split K, four tokens
+    (1, 2, 320, 200),
+    (1, 1, 256, 16384),
+    (3, 4, 1000, 1024),
 ]
 
 
@@ -127,6 +131,8 @@ def test_w4a16_launcher_call_shape(cuda_device, golden):
 # Decode shapes with activations of very different magnitude per token and per
 # 128-k block, all-zero tokens and blocks, and a K that is not a multiple of 128.
 @pytest.mark.parametrize("B,M,N,K,act_dtype", [
+    (1, 2, 512, 2048, torch.bfloat16),   # dp4a GEMV path: one large and one small token
+    (2, 3, 256, 640, torch.float16),
     (1, 7, 384, 200, torch.bfloat16),
     (3, 24, 640, 1152, torch.float16),
     (1, 9, 4096, 4096, torch.bfloat16),
