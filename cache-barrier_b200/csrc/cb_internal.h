@@ -130,6 +130,9 @@ struct W8A8Launch {
   size_t workspace_bytes;
 };
 int launch_w8a8(const W8A8Launch& L, cudaStream_t stream);
+// One token per batch entry: the dp4a GEMV kernel (w8a8_gemv.cu), no workspace.
+bool w8a8_gemv_eligible(const W8A8Launch& L);
+int launch_w8a8_gemv(const W8A8Launch& L, cudaStream_t stream);
 size_t w8a8_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K);
 
 struct W4A16Launch {
@@ -151,9 +154,11 @@ int launch_w4a16(const W4A16Launch& L, cudaStream_t stream);
 bool w4a16_resident_eligible(const W4A16Launch& L);
 int launch_w4a16_resident(const W4A16Launch& L, cudaStream_t stream);
 size_t w4a16_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K);
-// One to four tokens: the dp4a GEMV kernel (w4a16_gemv.cu) instead of the
-// tensor-core kernel; at most kGemvCtasPerSm CTAs per SM when it splits K.
-constexpr int kGemvMaxTokens = 4;
+// One or two tokens: the dp4a GEMV kernel (w4a16_gemv.cu) instead of the
+// tensor-core kernel (from four tokens on, the dp4a chains cost more than the
+// tensor cores' fixed MMA time: K = N = 8192, T = 4 took 41.9 us against
+// 28 us); at most kGemvCtasPerSm CTAs per SM when it splits K.
+constexpr int kGemvMaxTokens = 2;
 constexpr int kGemvCtasPerSm = 4;
 bool w4a16_gemv_eligible(const W4A16Launch& L);
 int launch_w4a16_gemv(const W4A16Launch& L, cudaStream_t stream);

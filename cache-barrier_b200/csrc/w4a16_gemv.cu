@@ -1,4 +1,4 @@
-// W4A16 for one to four tokens: int4 x 16-bit activations on the integer dot
+// W4A16 for one or two tokens: int4 x 16-bit activations on the integer dot
 // product units (dp4a) instead of the tensor cores.
 //
 // Math (kernel_batched_w4a16_simple, profiling/bench_l2_barrier.py:36-85, with
@@ -85,7 +85,7 @@ __device__ __forceinline__ uint32_t pack4(int b0, int b1, int b2, int b3) {
          ((static_cast<uint32_t>(b2) & 0xFFu) << 16) | ((static_cast<uint32_t>(b3) & 0xFFu) << 24);
 }
 
-// TM: tokens (1, 2 or 4); DEPTH: k-blocks of weights in flight per thread (4 for
+// TM: tokens (1 or 2); DEPTH: k-blocks of weights in flight per thread (4 for
 // long ranges, 1 when a CTA has one or two k-blocks and occupancy matters more)
 template <int TM, int DEPTH>
 __global__ void __launch_bounds__(kGvThreads) w4a16_gemv_kernel(const GvParams p) {
@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(kGvThreads) w4a16_gemv_kernel(const GvParams p
   // groups and write nothing.
   // loads in flight per thread: more for long ranges with few tokens; one where
   // occupancy (registers) matters more (one or two k-blocks per CTA)
-  constexpr int kGvRounds = DEPTH == 1 ? 1 : TM == 1 ? 4 : TM == 2 ? 2 : 1;
+  constexpr int kGvRounds = DEPTH == 1 ? 1 : TM == 1 ? 4 : 2;
   const int ngroups = nkb * 16;
   for (int base0 = 0; base0 < ngroups; base0 += kGvRounds * kGvThreads) {
     uint4 raw[kGvRounds][TM];
@@ -410,7 +410,7 @@ int launch_w4a16_gemv(const W4A16Launch& L, cudaStream_t stream) {
     g.counters = ws.counters;
   }
   const int kb_max = static_cast<int>((g.KB + ksplit - 1) / ksplit);
-  const int TM = g.M <= 1 ? 1 : g.M <= 2 ? 2 : 4;
+  const int TM = g.M <= 1 ? 1 : 2;
   const size_t smem = static_cast<size_t>(kb_max) * 16 * TM * 16 + static_cast<size_t>(kb_max) * TM * 4;
   if (smem > 200 * 1024) return CB_ERR_UNSUPPORTED;
   const bool deep = kb_max > 2;
@@ -418,12 +418,9 @@ int launch_w4a16_gemv(const W4A16Launch& L, cudaStream_t stream) {
     case 1:
       return deep ? launch_tm<1, 4>(g, static_cast<int>(grid), smem, stream)
                   : launch_tm<1, 1>(g, static_cast<int>(grid), smem, stream);
-    case 2:
+    default:
       return deep ? launch_tm<2, 4>(g, static_cast<int>(grid), smem, stream)
                   : launch_tm<2, 1>(g, static_cast<int>(grid), smem, stream);
-    default:
-      return deep ? launch_tm<4, 4>(g, static_cast<int>(grid), smem, stream)
-                  : launch_tm<4, 1>(g, static_cast<int>(grid), smem, stream);
   }
 }
 

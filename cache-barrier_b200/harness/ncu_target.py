@@ -28,7 +28,7 @@ from cb200 import ops  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["w8a8", "w8a8_dynamic", "w4a16", "nvfp4", "mla"], default="w8a8")
+    ap.add_argument("--op", choices=["w8a8", "w8a8_dynamic", "fp8", "w4a16", "nvfp4", "mla"], default="w8a8")
     ap.add_argument("--heads", type=int, default=16, help="mla: batch of heads (latents [heads, tokens, k])")
     ap.add_argument("--batch", type=int, default=1,
                     help="w8a8: batch of GEMMs (the reference's gate shapes: --batch 128 --k 128 --n 32*W)")
@@ -61,6 +61,19 @@ def main():
                 ops.w8a8_gemm(q, weights[i % args.copies], s, ws_, out=out)
             else:
                 ops.w8a8_gemm_dynamic(a, weights[i % args.copies], ws_, q=q, s=s, out=out)
+    elif args.op == "fp8":
+        # e4m3 x e4m3 per-token / per-channel (tcgen05.mma.kind::f8f6f4), fp32 accumulators
+        ws_ = ((torch.randn(N, generator=g, device=dev) * 0.01).abs() + 1e-4).float()
+        weights = []
+        for _ in range(args.copies):
+            w = (torch.randn(N, K, generator=g, device=dev) * 0.05).to(torch.bfloat16)
+            qw, _ = ops.quant_act_fp8(w)
+            weights.append(qw)
+            del w
+        qa, sa = ops.quant_act_fp8(a)
+
+        def run(i):
+            ops.fp8_gemm(qa, weights[i % args.copies], sa, ws_, out=out)
     elif args.op == "mla":
         # latent reconstruction: [heads, T, K] bf16 x int4 g128 [heads, K, N] (weight-stationary kernel)
         H = args.heads
