@@ -933,6 +933,7 @@ size_t w8a8_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K) {
 
 int launch_w8a8(const W8A8Launch& L, cudaStream_t stream) {
   if (L.batch == 0 || L.M == 0 || L.N == 0) return CB_OK;
+  if (w8a8_gemv_eligible(L)) return launch_w8a8_gemv(L, stream);
   const int TN = token_tile(L.M);
   Params p = {};
   p.M = static_cast<int>(L.M);

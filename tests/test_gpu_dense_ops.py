@@ -65,10 +65,11 @@ def test_cutlass_scaled_mm_int8_bit_exact(cuda_device, M, N, K, out_dtype, with_
     assert np.array_equal(out_bits(out), ref_bits)
 
 
-def test_cutlass_scaled_mm_per_tensor_scales_row_major_b(cuda_device):
+@pytest.mark.parametrize("M", [8, 1])
+def test_cutlass_scaled_mm_per_tensor_scales_row_major_b(cuda_device, M):
     """Per-tensor scale_a / scale_b (one element each), b row-major (copied to K-major), f32 bias."""
     import dense_ops
-    M, N, K = 8, 384, 768
+    N, K = 384, 768
     g = torch.Generator().manual_seed(77)
     aq = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int32).to(torch.int8)
     wq_kn = torch.randint(-127, 128, (K, N), generator=g, dtype=torch.int32).to(torch.int8)

@@ -47,9 +47,13 @@ SHAPES_G128 = [  # (B, M, N, K)
     (4, 1, 512, 128),
     (16, 512, 128, 512),
     (1, 32, 8192, 8192),
-    # one to four tokens take the dp4a GEMV kernel: ragged K and N, split K, four tokens
+    # one or two tokens take the dp4a GEMV kernel: ragged K and N, split K;
+    # more tiles than CTA slots (several n-tiles per CTA, ragged last tile);
+    # four tokens take the tensor cores
     (1, 2, 320, 200),
     (1, 1, 256, 16384),
+    (300, 2, 256, 256),
+    (4, 1, 40000, 128),
     (3, 4, 1000, 1024),
 ]
 
@@ -73,7 +77,8 @@ def test_w4a16_g128_bf16(cuda_device, B, M, N, K):
     assert ops.device_status(cuda_device) == 0
 
 
-@pytest.mark.parametrize("B,M,N,K", [(2, 3, 192, 256), (1, 1, 8192, 8192), (2, 33, 256, 1024), (128, 4, 512, 128)])
+@pytest.mark.parametrize("B,M,N,K", [(2, 3, 192, 256), (1, 1, 8192, 8192), (2, 33, 256, 1024), (128, 4, 512, 128),
+                                     (64, 1, 2048, 128)])
 def test_w4a16_per_channel_fp16(cuda_device, B, M, N, K):
     """Reference semantics: per-output-channel fp16 scale applied to the fp32 accumulator."""
     from cb200 import _lib as L

@@ -27,6 +27,15 @@ SHAPES = [  # (B, M, N, K)
     (16, 20, 1024, 256),   # two k-blocks per tile
     (1, 64, 1280, 2560),   # 64-token tiles with scales from the shared-memory ring, cut tiles
     (1, 8, 8192, 8192),
+    # one token per batch entry (the dp4a path): every row-blocking branch,
+    # K tails inside a k-step, row blocks that cross batch entries
+    (3, 1, 37, 48),
+    (1, 1, 333, 160),
+    (2, 1, 100, 272),
+    (2, 1, 130, 784),
+    (1, 1, 300, 1552),
+    (1, 1, 520, 4112),
+    (1, 1, 1000, 8208),
 ]
 
 
@@ -74,6 +83,25 @@ def test_w8a8_dynamic_equals_two_step(cuda_device, B, M, N, K):
     assert torch.equal(one.view(torch.int16), two.view(torch.int16))
     ref_out, _, _, _ = O.w8a8_dynamic(to_np_f32(a), wq.numpy(), ws.numpy(), "bf16")
     assert np.array_equal(out_bits(one), ref_out)
+
+
+def test_w8a8_one_token_batched_bias(cuda_device):
+    """One token per batch entry with a per-entry bias [B, N] and f32 output."""
+    from cb200 import ops
+    B, M, N, K = 3, 1, 70, 1040
+    a, wq, ws = _inputs(B, M, N, K, seed=31)
+    bias = torch.randn(B, N, generator=torch.Generator().manual_seed(32)).to(torch.bfloat16)
+    d = cuda_device
+    q, s = ops.quant_act_i8(a.to(d))
+    w_nk = ops.repack_w8_kmajor(wq.to(d))
+    acc = torch.empty(B, M, N, dtype=torch.int32, device=d)
+    out = ops.w8a8_gemm(q, w_nk, s, ws.to(d), out_dtype=torch.float32, acc_out=acc, bias=bias.to(d))
+    torch.cuda.synchronize()
+    ref_q, ref_s = O.quant_act_i8(to_np_f32(a))
+    ref_acc = O.gemm_i8_i32(ref_q, wq.numpy())
+    assert np.array_equal(acc.cpu().numpy(), ref_acc)
+    ref = O.w8a8_epilogue(ref_acc, ref_s, ws.numpy(), "f32", bias=to_np_f32(bias))
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
 
 
 def test_w8a8_strided_output_and_canary(cuda_device):
