@@ -7,8 +7,9 @@
 // computed as
 //   out = 2^-e_m * sum_{k-blocks j} s[j, n] * S_j,   S_j = sum_{k in j} q[k, n] * X[m, k]
 // where X = rint(a * 2^e_m) is a 15-bit fixed-point image of the token's row
-// (e_m from the row's amax, so that 2^13 <= amax * 2^e_m < 2^14: each element's
-// rounding error is at most 2^-15 of the row's amax), split exactly into two
+// (e_m from the amax of the row's part that the CTA sums, so that 2^13 <=
+// amax * 2^e_m < 2^14: each element's rounding error is at most 2^-15 of that
+// amax, at most the row's amax), split exactly into two
 // int8 halves X = 256 hi + lo. Each S_j is an exact int32 sum of dp4a products;
 // the weights enter dp4a as the unsigned bytes q + 8 of the native nibbles
 // (XOR 8), and 8 * sum X over the k-block is subtracted back. The group scale
@@ -27,8 +28,10 @@
 // contiguous range of k-blocks (split-K over the CTAs of a tile when there
 // are few tiles), or, when there are more tiles than CTA slots, several
 // n-tiles of one batch entry with all their k-blocks (the reference's gate
-// shapes, H = 128, K = 128, W = 128 MB: 14.8 -> 11.8 us at T = 1). Every CTA first reduces each token's amax over the whole row
-// (all CTAs of a row find the same e), then writes the fixed-point halves of
+// shapes, H = 128, K = 128, W = 128 MB: 14.8 -> 11.8 us at T = 1). Every CTA
+// first reduces each token's amax over its own k-range (the whole row unless
+// K is split: a split CTA reads 1/ksplit of the row instead of all of it, and
+// the second read of its part hits L1), then writes the fixed-point halves of
 // its own k-range into shared memory, permuted to the nibble order of the
 // native words (k0,k4,k1,k5 | k2,k6,k3,k7 per 8 k). The main loop streams the
 // weight rows with 16-byte global loads, up to four k-blocks in flight. A split tile
@@ -156,7 +159,10 @@ __global__ void __launch_bounds__(kGvThreads) w4a16_gemv_kernel(const GvParams p
   for (int d = 0; d < DEPTH; ++d) issue(buf[d], sbuf[d]);
   pdl_wait_primary();
 
-  // 1. per-token amax over the whole row -> fixed-point exponent
+  // 1. per-token amax over this CTA's k-range -> fixed-point exponent (the
+  // whole row unless K is split; the parts of a split tile are scaled by
+  // their own 2^-e, exactly, before they are summed)
+  const int k_lo = kb0 * kGvKb, k_hi = min(kb1 * kGvKb, p.K);
   const char* abase = static_cast<const char*>(p.a);
   float amax[TM];
 #pragma unroll
@@ -167,9 +173,9 @@ __global__ void __launch_bounds__(kGvThreads) w4a16_gemv_kernel(const GvParams p
       if (p.a_vec) {
         // eight 16-bit values per load, several loads in flight per thread
         const uint4* av = reinterpret_cast<const uint4*>(abase + off * 2);
-        const int nvec = p.K / 8;
+        const int nvec = k_hi / 8;
 #pragma unroll(DEPTH == 1 ? 1 : 8)
-        for (int i = tid; i < nvec; i += kGvThreads) {
+        for (int i = k_lo / 8 + tid; i < nvec; i += kGvThreads) {
           const uint4 u = __ldg(av + i);
           const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -182,7 +188,8 @@ __global__ void __launch_bounds__(kGvThreads) w4a16_gemv_kernel(const GvParams p
           }
         }
       } else {
-        for (int k = tid; k < p.K; k += kGvThreads) amax[m] = fmaxf(amax[m], fabsf(act_f32(abase, p.a_dtype, off + k)));
+        for (int k = k_lo + tid; k < k_hi; k += kGvThreads)
+          amax[m] = fmaxf(amax[m], fabsf(act_f32(abase, p.a_dtype, off + k)));
       }
     }
     for (int o = 16; o > 0; o >>= 1) amax[m] = fmaxf(amax[m], __shfl_xor_sync(0xffffffffu, amax[m], o));
@@ -276,7 +283,7 @@ __global__ void __launch_bounds__(kGvThreads) w4a16_gemv_kernel(const GvParams p
   __syncthreads();
 
   // 4. epilogue of n-tile t: out = v * s_channel * 2^-e
-  auto finish = [&](const float (&v)[TM], int t) {
+  auto finish = [&](const float (&v)[TM], int t, bool apply_ex) {
     const int n = (nt0 + t) * kGvRows + r;
     if (n >= p.N) return;
     const float sc = p.scale_at_end ? load_elem(p.scales, p.scale_dtype, h * p.s_sb + n) : 1.0f;
@@ -284,7 +291,7 @@ __global__ void __launch_bounds__(kGvThreads) w4a16_gemv_kernel(const GvParams p
     for (int m = 0; m < TM; ++m) {
       if (m < p.M) {
         float f = p.scale_at_end ? __fmul_rn(v[m], sc) : v[m];
-        f = ldexpf(f, -ex[m]);
+        if (apply_ex) f = ldexpf(f, -ex[m]);
         store_elem(p.out, p.out_dtype, h * p.out_sb + static_cast<long long>(m) * p.out_sm + n, f);
       }
     }
@@ -326,7 +333,7 @@ __global__ void __launch_bounds__(kGvThreads) w4a16_gemv_kernel(const GvParams p
         }
         issue(buf[d], sbuf[d]);
         if (MULTI && ++kbl == nkb) {  // n-tile ct complete
-          finish(acc, ct);
+          finish(acc, ct, true);
 #pragma unroll
           for (int m = 0; m < TM; ++m) acc[m] = 0.0f;
           kbl = 0;
@@ -339,14 +346,14 @@ __global__ void __launch_bounds__(kGvThreads) w4a16_gemv_kernel(const GvParams p
   }
   if (MULTI) return;
   if (p.ksplit == 1) {
-    finish(acc, 0);
+    finish(acc, 0, true);
     return;
   }
   // split tile (one n-tile per CTA): deterministic sum of the parts
   const long long tile = q;
   float* slot = p.partials + static_cast<long long>(blockIdx.x) * TM * kGvRows;
 #pragma unroll
-  for (int m = 0; m < TM; ++m) slot[m * kGvRows + r] = acc[m];
+  for (int m = 0; m < TM; ++m) slot[m * kGvRows + r] = ldexpf(acc[m], -ex[m]);
   __threadfence();
   __syncthreads();
   if (tid == 0) sh_last = atomicAdd(&p.counters[tile], 1) == p.ksplit - 1 ? 1 : 0;
@@ -361,7 +368,7 @@ __global__ void __launch_bounds__(kGvThreads) w4a16_gemv_kernel(const GvParams p
 #pragma unroll
     for (int m = 0; m < TM; ++m) sum[m] = __fadd_rn(sum[m], __ldcg(src + m * kGvRows + r));
   }
-  finish(sum, 0);
+  finish(sum, 0, false);
   if (tid == 0) p.counters[tile] = 0;  // next launch starts from zero
 }
 

@@ -22,6 +22,7 @@ the drop-in ``bench_l2_barrier.batched_int4_gemm`` instead of the Triton one.
 from __future__ import annotations
 
 import argparse
+import json
 import os
 import statistics
 import sys
@@ -101,6 +102,11 @@ def c_eff(l2_mb: float):
     return cliff, [(round(m, 1), round(b, 3)) for m, b in pts]
 
 
+# One token per batch entry runs the W4A16 dp4a GEMV (exact int4 weights, 15-bit
+# fixed-point activations, per-channel scale on the fp32 sum).
+R_DEQUANT_KERNEL = "cb200 w4a16_gemv_kernel (dp4a), per-channel scales, T=1"
+
+
 def r_dequant():
     import bench_l2_barrier as B
 
@@ -121,9 +127,24 @@ def r_dequant():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=None)
+    ap.add_argument("--only", choices=["all", "r_dequant"], default="all",
+                    help="r_dequant: re-measure only the dequant rate and update it in --out")
     args = ap.parse_args()
     torch.manual_seed(0)
     info = gpu_info()
+    if args.only == "r_dequant":
+        p = {}
+        if args.out and os.path.exists(args.out):
+            with open(args.out) as f:
+                p = json.load(f)
+        with ClockSampler(0) as clk:
+            rd, rd_times = r_dequant()
+        p.update({"r_dequant_tbs": round(rd, 4), "r_dequant_times_us": rd_times, "r_dequant_clocks": clk.info,
+                  "r_dequant_kernel": R_DEQUANT_KERNEL})
+        print(f"  r_dequant_tbs: {p['r_dequant_tbs']}  times {rd_times}", flush=True)
+        if args.out:
+            save_json(args.out, p)
+        return
     l2 = torch.cuda.get_device_properties(0).L2_cache_size / 2**20
     print(info, flush=True)
     with ClockSampler(0) as clk:
@@ -138,7 +159,7 @@ def main():
         p["r_dequant_tbs"] = round(rd, 4)
         p["r_dequant_times_us"] = rd_times
     p.update({"gpu": info, "nominal_l2_mb": round(l2, 1), "clocks": clk.info,
-              "r_dequant_kernel": "cb200 w4a16 (tcgen05 kind::f16), per-channel scales, T=1"})
+              "r_dequant_kernel": R_DEQUANT_KERNEL})
     for k, v in p.items():
         if k not in ("c_eff_curve_mb_tbs",):
             print(f"  {k}: {v}", flush=True)
