@@ -130,8 +130,8 @@ struct W8A8Launch {
   size_t workspace_bytes;
 };
 int launch_w8a8(const W8A8Launch& L, cudaStream_t stream);
-// One token per batch entry: the dp4a GEMV kernel (w8a8_gemv.cu); of the
-// workspace it uses only the status word.
+// One or two tokens per batch entry: the dp4a GEMV kernel (w8a8_gemv.cu); of
+// the workspace it uses only the status word.
 bool w8a8_gemv_eligible(const W8A8Launch& L);
 int launch_w8a8_gemv(const W8A8Launch& L, cudaStream_t stream);
 size_t w8a8_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K);

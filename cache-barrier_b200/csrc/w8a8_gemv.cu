@@ -1,5 +1,5 @@
-// W8A8 for a single token per batch entry (decode with T = 1): int8 x int8 on
-// the integer dot-product units (dp4a) instead of the tensor cores.
+// W8A8 for one or two tokens per batch entry (decode with T <= 2): int8 x int8
+// on the integer dot-product units (dp4a) instead of the tensor cores.
 //
 // Math (_w8a8_bmm_kernel, profiling/w8a8/w8a8_bmm.py:44-81):
 //   acc[n] = sum_k aq[k] * w[n, k]                  (int32, exact in any order)
@@ -51,19 +51,25 @@ constexpr int kDepthShort = 1;
 // HBM faster (K = N = 16384: 45.5 vs 47.9 us; H = 128, K = 128, N = 10240:
 // 43.7 vs 44.5 us); below it the GEMV's lower fixed cost wins.
 constexpr long long kGemvMaxWeightBytes = 128ll << 20;
+// Two tokens double the activation reads per weight chunk (L1 / load-unit
+// traffic), which costs more than the tensor-core kernel's fixed cost once the
+// weights are large: at 16 MiB (K = N = 4096) 6.4 vs 8.2 us, at 30 MiB
+// (K = 5120, N = 6144) 12.7 vs 10.8 us, at 64 MiB 19.6 vs 14.7 us.
+constexpr long long kGemv2MaxWeightBytes = 16ll << 20;
+constexpr int kW8GemvMaxTokens = 2;
 
 struct WgParams {
   const int8_t* aq;
-  long long aq_sb;
+  long long aq_sb, aq_sm;
   const float* a_scale;
-  long long as_sb;
+  long long as_sb, as_sm;
   const int8_t* w;
   long long w_sb, w_sn;
   const float* w_scale;
   long long ws_sb, ws_sn;
   void* out;
   int out_dtype;
-  long long out_sb;
+  long long out_sb, out_sm;
   int32_t* acc_out;
   int raw_f32;
   const void* bias;
@@ -93,7 +99,8 @@ __device__ __forceinline__ uint4 ld_stream16(const void* ptr) {
   return v;
 }
 
-template <int LPR, int KCH, int R, int D>
+// TM tokens (1 or 2) share each weight chunk.
+template <int LPR, int KCH, int R, int D, int TM>
 __global__ void __launch_bounds__(kWgThreads) w8a8_gemv_kernel(const WgParams p) {
   constexpr int kCh = R * KCH;            // chunks per lane per item
   constexpr int kRowsPerStep = 32 / LPR;  // rows covered by one chunk column of the warp
@@ -165,9 +172,11 @@ __global__ void __launch_bounds__(kWgThreads) w8a8_gemv_kernel(const WgParams p)
     __syncthreads();
     if (sh_abort) return;
   }
-  int acc[R];
+  int acc[R][TM];
 #pragma unroll
-  for (int r = 0; r < R; ++r) acc[r] = 0;
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int m = 0; m < TM; ++m) acc[r][m] = 0;
   int cj = 0, ck = 0;
   for (int base = 0; base < n_items; base += D + 1) {
 #pragma unroll
@@ -188,13 +197,16 @@ __global__ void __launch_bounds__(kWgThreads) w8a8_gemv_kernel(const WgParams p)
 #pragma unroll
         for (int c = 0; c < KCH; ++c) {
           const int k = k0 + c * 16 * LPR + li * 16;
-          const uint4 a =
-              (hh[r] >= 0 && k < p.K) ? __ldg(reinterpret_cast<const uint4*>(ar + k)) : make_uint4(0u, 0u, 0u, 0u);
           const uint4 w = ring[s][r * KCH + c];
-          acc[r] = dp4a_ss(w.x, a.x, acc[r]);
-          acc[r] = dp4a_ss(w.y, a.y, acc[r]);
-          acc[r] = dp4a_ss(w.z, a.z, acc[r]);
-          acc[r] = dp4a_ss(w.w, a.w, acc[r]);
+#pragma unroll
+          for (int m = 0; m < TM; ++m) {
+            const uint4 a = (hh[r] >= 0 && k < p.K) ? __ldg(reinterpret_cast<const uint4*>(ar + m * p.aq_sm + k))
+                                                    : make_uint4(0u, 0u, 0u, 0u);
+            acc[r][m] = dp4a_ss(w.x, a.x, acc[r][m]);
+            acc[r][m] = dp4a_ss(w.y, a.y, acc[r][m]);
+            acc[r][m] = dp4a_ss(w.z, a.z, acc[r][m]);
+            acc[r][m] = dp4a_ss(w.w, a.w, acc[r][m]);
+          }
         }
       }
       if (ks != nks - 1) continue;
@@ -203,36 +215,48 @@ __global__ void __launch_bounds__(kWgThreads) w8a8_gemv_kernel(const WgParams p)
 #pragma unroll
       for (int r = 0; r < R; ++r) {
 #pragma unroll
-        for (int o = LPR / 2; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+        for (int m = 0; m < TM; ++m) {
+#pragma unroll
+          for (int o = LPR / 2; o > 0; o >>= 1) acc[r][m] += __shfl_xor_sync(0xffffffffu, acc[r][m], o);
+        }
       }
-      int v = acc[0], h = hh[0], n = nn[0];
+      int v[TM], h = hh[0], n = nn[0];
+#pragma unroll
+      for (int m = 0; m < TM; ++m) v[m] = acc[0][m];
 #pragma unroll
       for (int r = 1; r < R; ++r) {
-        v = li == r ? acc[r] : v;
+#pragma unroll
+        for (int m = 0; m < TM; ++m) v[m] = li == r ? acc[r][m] : v[m];
         h = li == r ? hh[r] : h;
         n = li == r ? nn[r] : n;
       }
 #pragma unroll
-      for (int r = 0; r < R; ++r) acc[r] = 0;
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int m = 0; m < TM; ++m) acc[r][m] = 0;
       if (li >= R || h < 0) continue;
-      const long long oi = h * p.out_sb + n;
-      if (p.acc_out) p.acc_out[oi] = v;
-      float f = __int2float_rn(v);
-      if (!p.raw_f32) {
-        const float as = p.a_scale[h * p.as_sb];
-        const float ws = p.w_scale[h * p.ws_sb + static_cast<long long>(n) * p.ws_sn];
-        f = __fmul_rn(__fmul_rn(f, as), ws);
-        if (p.bias) f = __fadd_rn(f, load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n));
+      const float ws = p.raw_f32 ? 1.0f : p.w_scale[h * p.ws_sb + static_cast<long long>(n) * p.ws_sn];
+      const float bv = p.bias ? load_elem(p.bias, p.bias_dtype, h * p.bias_sb + n) : 0.0f;
+#pragma unroll
+      for (int m = 0; m < TM; ++m) {
+        const long long oi = h * p.out_sb + m * p.out_sm + n;
+        if (p.acc_out) p.acc_out[oi] = v[m];
+        float f = __int2float_rn(v[m]);
+        if (!p.raw_f32) {
+          const float as = p.a_scale[h * p.as_sb + m * p.as_sm];
+          f = __fmul_rn(__fmul_rn(f, as), ws);
+          if (p.bias) f = __fadd_rn(f, bv);
+        }
+        store_elem(p.out, p.out_dtype, oi, f);
       }
-      store_elem(p.out, p.out_dtype, oi, f);
     }
   }
 }
 
-template <int LPR, int KCH, int R, int D>
+template <int LPR, int KCH, int R, int D, int TM>
 int launch_cfg(const WgParams& g, cudaStream_t stream) {
   constexpr int kRb = R * (32 / LPR);
-  auto kern = w8a8_gemv_kernel<LPR, KCH, R, D>;
+  auto kern = w8a8_gemv_kernel<LPR, KCH, R, D, TM>;
   static int per_sm = 0;  // resident CTAs per SM (register-limited), looked up once
   if (per_sm == 0) {
     int v = 0;
@@ -258,15 +282,27 @@ int launch_cfg(const WgParams& g, cudaStream_t stream) {
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, g));
 }
 
+template <int TM>
+int launch_tm(const W8A8Launch& L, const WgParams& g, cudaStream_t stream) {
+  if (L.K > 2048) return launch_cfg<32, 8, 1, kDepthLong, TM>(g, stream);
+  if (L.K > 1024) return launch_cfg<32, 4, 2, kDepthShort, TM>(g, stream);
+  if (L.K > 512) return launch_cfg<32, 2, 4, kDepthShort, TM>(g, stream);
+  if (L.K > 256) return launch_cfg<32, 1, 8, kDepthShort, TM>(g, stream);
+  if (L.K > 128) return launch_cfg<16, 1, 8, kDepthShort, TM>(g, stream);
+  return launch_cfg<8, 1, 8, kDepthShort, TM>(g, stream);
+}
+
 }  // namespace
 
 bool w8a8_gemv_eligible(const W8A8Launch& L) {
-  // one token per batch entry, signed int8 operands, 16-byte aligned rows, at
-  // most kGemvMaxWeightBytes of weights (which keeps rows and items far below
-  // 2^31 for the 32-bit bookkeeping)
-  return L.M == 1 && !L.fp8 && !L.unsigned_operands && L.K % 16 == 0 && L.batch * L.N * L.K <= kGemvMaxWeightBytes &&
-         aligned16(L.aq) && aligned16(L.w) && L.w_sn % 16 == 0 &&
-         (L.batch == 1 || (L.w_sb % 16 == 0 && L.aq_sb % 16 == 0));
+  // one or two tokens per batch entry, signed int8 operands, 16-byte aligned
+  // rows, at most kGemvMaxWeightBytes (two tokens: kGemv2MaxWeightBytes) of
+  // weights, which also keeps rows and items far below 2^31 for the 32-bit
+  // bookkeeping
+  return L.M >= 1 && L.M <= kW8GemvMaxTokens && !L.fp8 && !L.unsigned_operands && L.K % 16 == 0 &&
+         L.batch * L.N * L.K <= (L.M == 1 ? kGemvMaxWeightBytes : kGemv2MaxWeightBytes) && aligned16(L.aq) &&
+         aligned16(L.w) && L.w_sn % 16 == 0 &&
+         (L.M == 1 || L.aq_sm % 16 == 0) && (L.batch == 1 || (L.w_sb % 16 == 0 && L.aq_sb % 16 == 0));
 }
 
 int launch_w8a8_gemv(const W8A8Launch& L, cudaStream_t stream) {
@@ -275,8 +311,10 @@ int launch_w8a8_gemv(const W8A8Launch& L, cudaStream_t stream) {
   WgParams g = {};
   g.aq = L.aq;
   g.aq_sb = L.aq_sb;
+  g.aq_sm = L.aq_sm;
   g.a_scale = L.a_scale;
   g.as_sb = L.as_sb;
+  g.as_sm = L.scale_per_tensor_a ? 0 : 1;
   g.w = L.w;
   g.w_sb = L.w_sb;
   g.w_sn = L.w_sn;
@@ -286,6 +324,7 @@ int launch_w8a8_gemv(const W8A8Launch& L, cudaStream_t stream) {
   g.out = L.out;
   g.out_dtype = L.out_dtype;
   g.out_sb = L.out_sb;
+  g.out_sm = L.out_sm;
   g.acc_out = L.acc_out;
   g.raw_f32 = L.raw_f32;
   g.bias = L.raw_f32 ? nullptr : L.bias;
@@ -298,12 +337,8 @@ int launch_w8a8_gemv(const W8A8Launch& L, cudaStream_t stream) {
   g.dbg_wait_ns = debug_wait_ns();
   // 4 KiB of weights per warp and item: one row slice of 4 KiB for long rows,
   // 8 rows x 512 B ... 32 rows x 128 B for short ones
-  if (L.K > 2048) return launch_cfg<32, 8, 1, kDepthLong>(g, stream);
-  if (L.K > 1024) return launch_cfg<32, 4, 2, kDepthShort>(g, stream);
-  if (L.K > 512) return launch_cfg<32, 2, 4, kDepthShort>(g, stream);
-  if (L.K > 256) return launch_cfg<32, 1, 8, kDepthShort>(g, stream);
-  if (L.K > 128) return launch_cfg<16, 1, 8, kDepthShort>(g, stream);
-  return launch_cfg<8, 1, 8, kDepthShort>(g, stream);
+  if (L.M == 1) return launch_tm<1>(L, g, stream);
+  return launch_tm<2>(L, g, stream);
 }
 
 }  // namespace cb

@@ -65,7 +65,7 @@ def test_cutlass_scaled_mm_int8_bit_exact(cuda_device, M, N, K, out_dtype, with_
     assert np.array_equal(out_bits(out), ref_bits)
 
 
-@pytest.mark.parametrize("M", [8, 1])
+@pytest.mark.parametrize("M", [8, 2, 1])
 def test_cutlass_scaled_mm_per_tensor_scales_row_major_b(cuda_device, M):
     """Per-tensor scale_a / scale_b (one element each), b row-major (copied to K-major), f32 bias."""
     import dense_ops

@@ -36,6 +36,10 @@ SHAPES = [  # (B, M, N, K)
     (1, 1, 300, 1552),
     (1, 1, 520, 4112),
     (1, 1, 1000, 8208),
+    # two tokens per batch entry (the dp4a path's two-token kernels)
+    (3, 2, 37, 48),
+    (2, 2, 130, 784),
+    (1, 2, 520, 4112),
 ]
 
 
