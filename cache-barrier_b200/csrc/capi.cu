@@ -399,8 +399,6 @@ int cb_w8a8_gemm_dynamic(const void* a, int a_dtype, int8_t* q_buf, float* s_buf
   const size_t need = w8a8_workspace_bytes(batch, M, N, K);
   if (!workspace || workspace_bytes < need) return CB_ERR_WORKSPACE;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  int r = launch_act_quant(a, a_dtype, batch, M, K, strides[0], strides[1], q_buf, M * K, K, s_buf, M, s);
-  if (r != CB_OK) return r;
   W8A8Launch L = {};
   L.aq = q_buf;
   L.a_scale = s_buf;
@@ -423,6 +421,12 @@ int cb_w8a8_gemm_dynamic(const void* a, int a_dtype, int8_t* q_buf, float* s_buf
   L.ws_sb = strides[6];
   L.workspace = workspace;
   L.workspace_bytes = workspace_bytes;
+  // One token of a single GEMM with a short row: the GEMV quantizes the row
+  // itself (same arithmetic, q and scale still stored to q_buf / s_buf), one
+  // launch.
+  if (w8a8_gemv_dynamic_eligible(L, a, a_dtype, strides[1])) return launch_w8a8_gemv_dynamic(L, a, a_dtype, strides[1], s);
+  int r = launch_act_quant(a, a_dtype, batch, M, K, strides[0], strides[1], q_buf, M * K, K, s_buf, M, s);
+  if (r != CB_OK) return r;
   return launch_w8a8(L, s);
 }
 

@@ -134,6 +134,11 @@ int launch_w8a8(const W8A8Launch& L, cudaStream_t stream);
 // the workspace it uses only the status word.
 bool w8a8_gemv_eligible(const W8A8Launch& L);
 int launch_w8a8_gemv(const W8A8Launch& L, cudaStream_t stream);
+// Dynamic quantization fused into the GEMV (one token of a single GEMM, short
+// rows): the kernel quantizes the 16-bit row a itself and stores q / scale to
+// L.aq / L.a_scale.
+bool w8a8_gemv_dynamic_eligible(const W8A8Launch& L, const void* a, int a_dtype, int64_t a_sm);
+int launch_w8a8_gemv_dynamic(const W8A8Launch& L, const void* a, int a_dtype, int64_t a_sm, cudaStream_t stream);
 size_t w8a8_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K);
 
 struct W4A16Launch {

@@ -57,6 +57,13 @@ constexpr long long kGemvMaxWeightBytes = 128ll << 20;
 // (K = 5120, N = 6144) 12.7 vs 10.8 us, at 64 MiB 19.6 vs 14.7 us.
 constexpr long long kGemv2MaxWeightBytes = 16ll << 20;
 constexpr int kW8GemvMaxTokens = 2;
+// Longest row quantized inside the GEMV (FUSE, one token). Every CTA
+// quantizes the whole row while its first weight items are in flight; for long
+// rows that work (two passes over the row, one IEEE division per element)
+// delays the weight stream more than a separate quantizer launch costs, whose
+// dependent GEMM starts streaming while it runs: K = 256 2.7 vs 3.9 us, K =
+// 1024 3.2 vs 3.7 us, K = 4096 7.2 vs 7.3 us, K = 8192 17.6 vs 15.4 us.
+constexpr int kFuseMaxRowBytes = 1024;
 
 struct WgParams {
   const int8_t* aq;
@@ -79,6 +86,12 @@ struct WgParams {
   int rows;                        // batch * N
   int* status;                     // the workspace's status word
   unsigned long long dbg_wait_ns;  // test hook: nonzero = wait this long on a flag nothing sets
+  // FUSE: the 16-bit activation rows (batch of one) quantized by every CTA
+  const void* a;
+  int a_dtype;
+  long long a_sm;
+  int8_t* q_out;  // the quantized rows and their scales, written by CTA 0
+  float* s_out;
 };
 
 __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
@@ -99,9 +112,32 @@ __device__ __forceinline__ uint4 ld_stream16(const void* ptr) {
   return v;
 }
 
-// TM tokens (1 or 2) share each weight chunk.
-template <int LPR, int KCH, int R, int D, int TM>
+__device__ __forceinline__ float act16_f32(uint32_t half_bits, int dtype) {
+  return dtype == CB_DTYPE_BF16 ? __uint_as_float(half_bits << 16)
+                                : __half2float(__ushort_as_half(static_cast<unsigned short>(half_bits)));
+}
+
+// Per-token int8 quantization with _quant_act_kernel's arithmetic
+// (profiling/w8a8/w8a8_bmm.py:30-41), the same operations as act_quant.cu:
+// scale = max(amax / 127, 1e-8), q = trunc(a / scale + 0.5 sign(a)).
+__device__ __forceinline__ uint32_t quant4(float x0, float x1, float x2, float x3, float sc) {
+  auto q1 = [sc](float x) {
+    const float y = __fadd_rn(__fdiv_rn(x, sc), x >= 0.0f ? 0.5f : -0.5f);
+    return static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(__float2int_rz(y))));
+  };
+  return q1(x0) | (q1(x1) << 8) | (q1(x2) << 16) | (q1(x3) << 24);
+}
+
+// TM tokens (1 or 2) share each weight chunk. FUSE (one token of a single
+// GEMM, short rows): every CTA quantizes the 16-bit token row itself into
+// shared memory after the dependency wait, while its first weight items are in
+// flight, instead of a separate quantizer launch; CTA 0 also stores q and the
+// scale.
+template <int LPR, int KCH, int R, int D, int TM, bool FUSE>
 __global__ void __launch_bounds__(kWgThreads) w8a8_gemv_kernel(const WgParams p) {
+  extern __shared__ __align__(16) int8_t gv_q[];  // FUSE: [TM][K] quantized rows
+  __shared__ float gv_red[kWgThreads / 32][TM];
+  __shared__ float gv_scale[TM];
   constexpr int kCh = R * KCH;            // chunks per lane per item
   constexpr int kRowsPerStep = 32 / LPR;  // rows covered by one chunk column of the warp
   constexpr int kRb = R * kRowsPerStep;   // rows per item
@@ -172,6 +208,54 @@ __global__ void __launch_bounds__(kWgThreads) w8a8_gemv_kernel(const WgParams p)
     __syncthreads();
     if (sh_abort) return;
   }
+  if constexpr (FUSE) {
+    // amax of each row (16-byte vectors, K % 8 == 0), then quantize from L1
+    const int nv = p.K / 8;
+    const int lane0 = threadIdx.x & 31, wq = threadIdx.x >> 5;
+#pragma unroll
+    for (int m = 0; m < TM; ++m) {
+      const uint4* av = reinterpret_cast<const uint4*>(static_cast<const char*>(p.a) + m * p.a_sm * 2);
+      float amax = 0.0f;
+#pragma unroll 8
+      for (int v = threadIdx.x; v < nv; v += kWgThreads) {
+        const uint4 u = __ldg(av + v);
+        const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          amax = fmaxf(amax, fmaxf(fabsf(act16_f32(wd[j] & 0xFFFFu, p.a_dtype)), fabsf(act16_f32(wd[j] >> 16, p.a_dtype))));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (lane0 == 0) gv_red[wq][m] = amax;
+    }
+    __syncthreads();
+    if (threadIdx.x < TM) {
+      float amax = gv_red[0][threadIdx.x];
+#pragma unroll
+      for (int w = 1; w < kWgThreads / 32; ++w) amax = fmaxf(amax, gv_red[w][threadIdx.x]);
+      const float sc = fmaxf(__fdiv_rn(amax, 127.0f), 1e-8f);
+      gv_scale[threadIdx.x] = sc;
+      if (blockIdx.x == 0) p.s_out[threadIdx.x] = sc;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < TM; ++m) {
+      const uint4* av = reinterpret_cast<const uint4*>(static_cast<const char*>(p.a) + m * p.a_sm * 2);
+      const float sc = gv_scale[m];
+#pragma unroll 8
+      for (int v = threadIdx.x; v < nv; v += kWgThreads) {
+        const uint4 u = __ldg(av + v);
+        uint2 qv;
+        qv.x = quant4(act16_f32(u.x & 0xFFFFu, p.a_dtype), act16_f32(u.x >> 16, p.a_dtype),
+                      act16_f32(u.y & 0xFFFFu, p.a_dtype), act16_f32(u.y >> 16, p.a_dtype), sc);
+        qv.y = quant4(act16_f32(u.z & 0xFFFFu, p.a_dtype), act16_f32(u.z >> 16, p.a_dtype),
+                      act16_f32(u.w & 0xFFFFu, p.a_dtype), act16_f32(u.w >> 16, p.a_dtype), sc);
+        *reinterpret_cast<uint2*>(gv_q + m * p.K + v * 8) = qv;
+        if (blockIdx.x == 0) *reinterpret_cast<uint2*>(p.q_out + m * p.aq_sm + v * 8) = qv;
+      }
+    }
+    __syncthreads();
+  }
   int acc[R][TM];
 #pragma unroll
   for (int r = 0; r < R; ++r)
@@ -200,8 +284,10 @@ __global__ void __launch_bounds__(kWgThreads) w8a8_gemv_kernel(const WgParams p)
           const uint4 w = ring[s][r * KCH + c];
 #pragma unroll
           for (int m = 0; m < TM; ++m) {
-            const uint4 a = (hh[r] >= 0 && k < p.K) ? __ldg(reinterpret_cast<const uint4*>(ar + m * p.aq_sm + k))
-                                                    : make_uint4(0u, 0u, 0u, 0u);
+            uint4 a = make_uint4(0u, 0u, 0u, 0u);
+            if (hh[r] >= 0 && k < p.K)
+              a = FUSE ? *reinterpret_cast<const uint4*>(gv_q + m * p.K + k)
+                       : __ldg(reinterpret_cast<const uint4*>(ar + m * p.aq_sm + k));
             acc[r][m] = dp4a_ss(w.x, a.x, acc[r][m]);
             acc[r][m] = dp4a_ss(w.y, a.y, acc[r][m]);
             acc[r][m] = dp4a_ss(w.z, a.z, acc[r][m]);
@@ -243,7 +329,7 @@ __global__ void __launch_bounds__(kWgThreads) w8a8_gemv_kernel(const WgParams p)
         if (p.acc_out) p.acc_out[oi] = v[m];
         float f = __int2float_rn(v[m]);
         if (!p.raw_f32) {
-          const float as = p.a_scale[h * p.as_sb + m * p.as_sm];
+          const float as = FUSE ? gv_scale[m] : p.a_scale[h * p.as_sb + m * p.as_sm];
           f = __fmul_rn(__fmul_rn(f, as), ws);
           if (p.bias) f = __fadd_rn(f, bv);
         }
@@ -253,14 +339,18 @@ __global__ void __launch_bounds__(kWgThreads) w8a8_gemv_kernel(const WgParams p)
   }
 }
 
-template <int LPR, int KCH, int R, int D, int TM>
+template <int LPR, int KCH, int R, int D, int TM, bool FUSE>
 int launch_cfg(const WgParams& g, cudaStream_t stream) {
   constexpr int kRb = R * (32 / LPR);
-  auto kern = w8a8_gemv_kernel<LPR, KCH, R, D, TM>;
-  static int per_sm = 0;  // resident CTAs per SM (register-limited), looked up once
+  auto kern = w8a8_gemv_kernel<LPR, KCH, R, D, TM, FUSE>;
+  const size_t smem = FUSE ? static_cast<size_t>(TM) * g.K : 0;
+  static int per_sm = 0;  // resident CTAs per SM, looked up once (at the largest fused row)
   if (per_sm == 0) {
     int v = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kern, kWgThreads, 0) != cudaSuccess || v <= 0) v = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kern, kWgThreads, FUSE ? kFuseMaxRowBytes : 0) !=
+            cudaSuccess ||
+        v <= 0)
+      v = 1;
     per_sm = v;
   }
   const int sms = sm_count();
@@ -272,7 +362,7 @@ int launch_cfg(const WgParams& g, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(kWgThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -282,14 +372,14 @@ int launch_cfg(const WgParams& g, cudaStream_t stream) {
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, g));
 }
 
-template <int TM>
+template <int TM, bool FUSE>
 int launch_tm(const W8A8Launch& L, const WgParams& g, cudaStream_t stream) {
-  if (L.K > 2048) return launch_cfg<32, 8, 1, kDepthLong, TM>(g, stream);
-  if (L.K > 1024) return launch_cfg<32, 4, 2, kDepthShort, TM>(g, stream);
-  if (L.K > 512) return launch_cfg<32, 2, 4, kDepthShort, TM>(g, stream);
-  if (L.K > 256) return launch_cfg<32, 1, 8, kDepthShort, TM>(g, stream);
-  if (L.K > 128) return launch_cfg<16, 1, 8, kDepthShort, TM>(g, stream);
-  return launch_cfg<8, 1, 8, kDepthShort, TM>(g, stream);
+  if (L.K > 2048) return launch_cfg<32, 8, 1, kDepthLong, TM, FUSE>(g, stream);
+  if (L.K > 1024) return launch_cfg<32, 4, 2, kDepthShort, TM, FUSE>(g, stream);
+  if (L.K > 512) return launch_cfg<32, 2, 4, kDepthShort, TM, FUSE>(g, stream);
+  if (L.K > 256) return launch_cfg<32, 1, 8, kDepthShort, TM, FUSE>(g, stream);
+  if (L.K > 128) return launch_cfg<16, 1, 8, kDepthShort, TM, FUSE>(g, stream);
+  return launch_cfg<8, 1, 8, kDepthShort, TM, FUSE>(g, stream);
 }
 
 }  // namespace
@@ -305,9 +395,8 @@ bool w8a8_gemv_eligible(const W8A8Launch& L) {
          (L.M == 1 || L.aq_sm % 16 == 0) && (L.batch == 1 || (L.w_sb % 16 == 0 && L.aq_sb % 16 == 0));
 }
 
-int launch_w8a8_gemv(const W8A8Launch& L, cudaStream_t stream) {
-  // no split-K scratch: only the status word of the caller's workspace is used
-  if (L.workspace == nullptr || L.workspace_bytes < kWsHeader) return CB_ERR_WORKSPACE;
+namespace {
+WgParams gemv_params(const W8A8Launch& L) {
   WgParams g = {};
   g.aq = L.aq;
   g.aq_sb = L.aq_sb;
@@ -335,10 +424,38 @@ int launch_w8a8_gemv(const W8A8Launch& L, cudaStream_t stream) {
   g.rows = static_cast<int>(L.batch * L.N);
   g.status = static_cast<int*>(L.workspace);
   g.dbg_wait_ns = debug_wait_ns();
+  return g;
+}
+}  // namespace
+
+int launch_w8a8_gemv(const W8A8Launch& L, cudaStream_t stream) {
+  // no split-K scratch: only the status word of the caller's workspace is used
+  if (L.workspace == nullptr || L.workspace_bytes < kWsHeader) return CB_ERR_WORKSPACE;
+  const WgParams g = gemv_params(L);
   // 4 KiB of weights per warp and item: one row slice of 4 KiB for long rows,
   // 8 rows x 512 B ... 32 rows x 128 B for short ones
-  if (L.M == 1) return launch_tm<1>(L, g, stream);
-  return launch_tm<2>(L, g, stream);
+  if (L.M == 1) return launch_tm<1, false>(L, g, stream);
+  return launch_tm<2, false>(L, g, stream);
+}
+
+bool w8a8_gemv_dynamic_eligible(const W8A8Launch& L, const void* a, int a_dtype, int64_t a_sm) {
+  // one token of a single GEMM, a 16-bit row read as 16-byte vectors and at
+  // most kFuseMaxRowBytes long; L.aq / L.a_scale are the q and scale outputs
+  (void)a_sm;
+  return L.batch == 1 && L.M == 1 && w8a8_gemv_eligible(L) &&
+         (a_dtype == CB_DTYPE_BF16 || a_dtype == CB_DTYPE_F16) && L.K % 8 == 0 && aligned16(a) &&
+         L.K <= kFuseMaxRowBytes && !L.scale_per_tensor_a && !L.raw_f32;
+}
+
+int launch_w8a8_gemv_dynamic(const W8A8Launch& L, const void* a, int a_dtype, int64_t a_sm, cudaStream_t stream) {
+  if (L.workspace == nullptr || L.workspace_bytes < kWsHeader) return CB_ERR_WORKSPACE;
+  WgParams g = gemv_params(L);
+  g.a = a;
+  g.a_dtype = a_dtype;
+  g.a_sm = a_sm;
+  g.q_out = const_cast<int8_t*>(L.aq);
+  g.s_out = const_cast<float*>(L.a_scale);
+  return launch_tm<1, true>(L, g, stream);
 }
 
 }  // namespace cb

@@ -163,10 +163,12 @@ CB_API int cb_w8a8_gemm_bias(const int8_t* aq, const float* a_scale, const int8_
 
 /* Dynamic per-token activation quantization followed by the W8A8 GEMM, two
    launches chained with programmatic dependent launch so the GEMM's weight
-   stream starts while the quantization runs. Replaces w8a8_bmm_full
+   stream starts while the quantization runs (one launch for one token of a
+   single GEMM with K <= 1024: the GEMV quantizes the row itself, with the same
+   arithmetic). Replaces w8a8_bmm_full
    (profiling/w8a8/w8a8_bmm.py:143-149). q_buf / s_buf are caller buffers that
    receive the quantized activations (int8 [batch, M, K] contiguous) and scales
-   (fp32 [batch * M]), as the reference's `bufs`.
+   (fp32 [batch * M]), as the reference's `bufs`, in both cases.
    strides (elements): {a_b, a_m, w_b, w_n, out_b, out_m, w_scale_b}. */
 CB_API int cb_w8a8_gemm_dynamic(const void* a, int a_dtype, int8_t* q_buf, float* s_buf, const int8_t* w,
                          const float* w_scale, void* out, int out_dtype, int64_t batch, int64_t M, int64_t N,

@@ -74,7 +74,8 @@ def test_w8a8_bit_exact(cuda_device, B, M, N, K, out_dtype):
     assert ops.device_status(cuda_device) == 0
 
 
-@pytest.mark.parametrize("B,M,N,K", [(1, 1, 8192, 8192), (1, 32, 8192, 8192), (2, 17, 640, 1280)])
+@pytest.mark.parametrize("B,M,N,K", [(1, 1, 8192, 8192), (1, 32, 8192, 8192), (2, 17, 640, 1280),
+                                     (1, 2, 1000, 4112), (1, 1, 333, 160), (1, 1, 96, 1024)])
 def test_w8a8_dynamic_equals_two_step(cuda_device, B, M, N, K):
     from cb200 import ops
     a, wq, ws = _inputs(B, M, N, K, seed=77 + M)
@@ -87,6 +88,30 @@ def test_w8a8_dynamic_equals_two_step(cuda_device, B, M, N, K):
     assert torch.equal(one.view(torch.int16), two.view(torch.int16))
     ref_out, _, _, _ = O.w8a8_dynamic(to_np_f32(a), wq.numpy(), ws.numpy(), "bf16")
     assert np.array_equal(out_bits(one), ref_out)
+
+
+@pytest.mark.parametrize("M,K,act_dtype", [(1, 1024, torch.bfloat16), (1, 256, torch.float16),
+                                           (1, 8192, torch.bfloat16), (2, 1040, torch.float16)])
+def test_w8a8_dynamic_fused_quant_outputs(cuda_device, M, K, act_dtype):
+    """One token of one GEMM with K <= 1024 quantizes inside the GEMV; with it
+    and with the separate quantizer (longer rows, two tokens) the q and scale
+    buffers the caller passes receive the quantizer's exact values, and a
+    second call with new activations overwrites them."""
+    from cb200 import ops
+    N = 520
+    d = cuda_device
+    q = torch.full((M, K), 99, dtype=torch.int8, device=d)
+    s = torch.full((M,), -1.0, dtype=torch.float32, device=d)
+    for seed in (41, 42):
+        a, wq, ws = _inputs(1, M, N, K, seed=seed, act_dtype=act_dtype)
+        w_nk = ops.repack_w8_kmajor(wq[0].to(d))
+        out = ops.w8a8_gemm_dynamic(a[0].to(d), w_nk, ws[0].to(d), q=q, s=s, out_dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        ref_out, ref_q, ref_s, _ = O.w8a8_dynamic(to_np_f32(a), wq.numpy(), ws.numpy(), "bf16")
+        assert np.array_equal(q.cpu().numpy(), ref_q.reshape(M, K))
+        assert np.array_equal(s.cpu().numpy().view(np.uint32), ref_s.reshape(-1).view(np.uint32))
+        assert np.array_equal(out_bits(out), ref_out.reshape(M, N))
+    assert ops.device_status(d) == 0
 
 
 def test_w8a8_one_token_batched_bias(cuda_device):
