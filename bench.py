@@ -324,6 +324,7 @@ def main():
     achieved_gbs = alg_bytes / (us_kernel * 1e-6) / 1e9
     peaks, peak_src = measured_peaks()
     traffic = committed_traffic("w8a8_gemm_k8192_n8192.json")
+    traffic_gemv = committed_traffic("w8a8_gemv_k8192_n8192_t1.json")
 
     # per-T kernel time (graph of CYCLES launches of one T)
     per_t = {}
@@ -583,7 +584,10 @@ def main():
                          "kernel": "w8a8_gemm_kernel (tcgen05 kind::i8) at T = 8/16/32, "
                                    "w8a8_gemv_kernel (dp4a) at T = 1",
                          "alg_bytes_per_launch": int(alg_bytes), "us_per_launch": round(us_kernel, 3),
-                         "traffic": (traffic or {}).get("dram_bytes_per_launch")},
+                         "traffic": (traffic or {}).get("dram_bytes_per_launch"),
+                         "traffic_by_kernel": {
+                             "w8a8_gemm_kernel (T=16 capture)": (traffic or {}).get("dram_bytes_per_launch"),
+                             "w8a8_gemv_kernel (T=1 capture)": (traffic_gemv or {}).get("dram_bytes_per_launch")}},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_us, 3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "cb_exec_w8a8_dynamic_host (C ABI, pinned host activations in and fp16 results out "
