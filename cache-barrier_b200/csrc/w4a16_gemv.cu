@@ -8,8 +8,8 @@
 //   out = 2^-e_m * sum_{k-blocks j} s[j, n] * S_j,   S_j = sum_{k in j} q[k, n] * X[m, k]
 // where X = rint(a * 2^e_m) is a 15-bit fixed-point image of the token's row
 // (e_m from the amax of the row's part that the CTA sums, so that 2^13 <=
-// amax * 2^e_m < 2^14: each element's rounding error is at most 2^-15 of that
-// amax, at most the row's amax), split exactly into two
+// amax * 2^e_m < 2^14: each element's rounding error is half a step, at most
+// 2^-14 of that amax, which is at most the row's amax), split exactly into two
 // int8 halves X = 256 hi + lo. Each S_j is an exact int32 sum of dp4a products;
 // the weights enter dp4a as the unsigned bytes q + 8 of the native nibbles
 // (XOR 8), and 8 * sum X over the k-block is subtracted back. The group scale

@@ -14,6 +14,11 @@ dequant (profiling/gate/bench_capacity_gate.py:235-244) with the scale indexed
 per group, and that case alone is "parity unpinned" beyond the per-channel
 pinning.
 
+The fixed-point restatement of the one- and two-token W4A16 GEMV
+(``w4a16_fixed_point_parts`` / ``w4a16_fixed_point_gemv``) has no counterpart in
+the reference: it states this library's own numerical method, and
+``tests/test_oracle_fixed_point.py`` checks it against the exact product.
+
 Exactness: integer GEMMs are computed as float64 matmuls of int8-valued arrays,
 which is exact while every partial sum stays below 2**53 (|sum| <= 127*127*K for
 K < 5e11).
@@ -173,6 +178,53 @@ def w4a16_per_channel(a_f32: np.ndarray, q: np.ndarray, scale_n: np.ndarray) -> 
     (profiling/bench_l2_barrier.py:78-82). scale_n [..., N]."""
     acc = np.matmul(np.asarray(a_f32, dtype=np.float64), q.astype(np.float64))
     return (acc.astype(np.float32) * np.asarray(scale_n, dtype=np.float32)[..., None, :]).astype(np.float32)
+
+
+def w4a16_fixed_point_parts(a_f32: np.ndarray, group_k0: int, group_k1: int):
+    """The one- and two-token GEMV's activation image of a[:, k0:k1] (one CTA's
+    k-range): exponent e per token from the range's amax (2^13 <= amax * 2^e <
+    2^14), X = rint(a * 2^e) and its exact split X = 256 * hi + lo with lo in
+    [-128, 127]. Returns (X, hi, lo, e) with X/hi/lo int64 [M, k1 - k0]."""
+    a = np.asarray(a_f32, dtype=np.float32)[:, group_k0:group_k1]
+    amax = np.abs(a).max(axis=1) if a.shape[1] else np.zeros(a.shape[0], np.float32)
+    _, E = np.frexp(amax)
+    e = np.where(amax > 0, 14 - E, 0).astype(np.int64)
+    X = np.rint(np.ldexp(a.astype(np.float64), e[:, None])).astype(np.int64)  # exact scaling, round half even
+    hi = (X + 128) >> 8
+    lo = X - 256 * hi
+    return X, hi, lo, e
+
+
+def w4a16_fixed_point_gemv(a_f32: np.ndarray, q: np.ndarray, scales: np.ndarray, group_size: int,
+                           ksplit: int = 1) -> np.ndarray:
+    """Restatement of the dp4a GEMV's arithmetic (one or two tokens): per K-split
+    part, exact integer sums S_j = sum_k q * X over each 128-k block, accumulated
+    as acc += s_j * S_j (fp32, per-group scales; a per-channel scale multiplies
+    the sum instead), scaled by 2^-e of the part, parts added in order.
+    a [M, K] fp32, q [K, N] int in [-8, 7], scales [G, N]. fp32 [M, N]."""
+    a = np.asarray(a_f32, dtype=np.float32)
+    M, K = a.shape
+    N = q.shape[1]
+    KB = -(-K // 128)
+    per_channel = group_size >= K
+    s = np.asarray(scales, dtype=np.float32)
+    out = np.zeros((M, N), dtype=np.float32)
+    for ks in range(ksplit):
+        kb0, kb1 = ks * KB // ksplit, (ks + 1) * KB // ksplit
+        X, _, _, e = w4a16_fixed_point_parts(a, kb0 * 128, min(kb1 * 128, K))
+        acc = np.zeros((M, N), dtype=np.float32)
+        for j in range(kb0, kb1):
+            k0, k1 = j * 128, min(j * 128 + 128, K)
+            S = X[:, k0 - kb0 * 128:k1 - kb0 * 128] @ q[k0:k1].astype(np.int64)  # exact
+            sc = np.float32(1.0) if per_channel else s[(j * 128) // group_size]
+            acc = (acc.astype(np.float64) + np.float64(1.0) * sc * S.astype(np.float64)).astype(np.float32)
+        if per_channel and ksplit == 1:
+            acc = (acc * s[0]).astype(np.float32)
+        part = np.ldexp(acc, -e[:, None]).astype(np.float32)
+        out = (out + part).astype(np.float32)
+    if per_channel and ksplit > 1:
+        out = (out * s[0]).astype(np.float32)
+    return out
 
 
 # ---------------------------------------------------------------------------
